@@ -1,0 +1,106 @@
+// cbq_common.cuh -- device helpers shared by the codebook decode-matmul kernels
+// (sm_100a): mbarrier + 1-D bulk-copy (TMA) staging, bounded waits, dtype I/O.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/cbq.h"
+
+namespace cbq {
+
+constexpr int kThreads = 256;            // threads per CTA of the GEMV kernels
+constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s bound on any device-side wait
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+                 ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+
+// Wait for phase `parity` of `bar` to complete, giving up after kWaitNs.
+// Returns false on timeout (the caller records CBQ_FLAG_TIMEOUT and stops).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (global_timer_ns() - t0 > kWaitNs) return false;
+    }
+}
+
+// 1-D bulk copy global -> this CTA's shared memory, completing on `bar`.
+// dst, src 16-byte aligned; bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes,
+                                         uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+
+template <typename T> __device__ __forceinline__ float to_f32(T v);
+template <> __device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
+    return __bfloat162float(v);
+}
+template <typename T> __device__ __forceinline__ T from_f32(float v);
+template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
+    return __float2bfloat16_rn(v);
+}
+
+// Record a decode error in the caller's status word (may be null).
+__device__ __forceinline__ void report(uint32_t *status, uint32_t flag, uint32_t row) {
+    if (!status) return;
+    atomicOr(status + CBQ_STATUS_FLAGS, flag);
+    atomicMin(status + CBQ_STATUS_FIRST_ROW, row);
+    atomicAdd(status + CBQ_STATUS_COUNT, 1u);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+}  // namespace cbq
+
+// Host-side helpers shared by the .cu files.
+namespace cbq_host {
+int sm_count();           // SMs of the current device (cached per device)
+int max_smem_optin();     // opt-in dynamic shared memory per block
+inline int64_t align_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
+}  // namespace cbq_host
+
+#define CBQ_CUDA_TRY(expr)                                   \
+    do {                                                     \
+        cudaError_t e_ = (expr);                             \
+        if (e_ != cudaSuccess) return CBQ_ERR_CUDA;          \
+    } while (0)

@@ -1,0 +1,189 @@
+/*
+ * cbq.h -- C ABI of the B200 codebook decode-matmul library (libcbq.so).
+ *
+ * Computes out = x @ W^T where W[r,k] = codebook[min(idx(r*K+k), C-1)] is
+ * never materialised: every call reads the compressed index stream itself.
+ * Two stream formats are accepted, both byte-for-byte the reference's
+ * on-disk `.npz` payloads (bigattichouse/Codebook-Quantization):
+ *
+ *   fixed width  `indices`: LSB-first, b bits per index (src/bitpack.py:32-94)
+ *   Huffman      `huff_stream` + `huff_lengths` + `huff_row_bit_starts`:
+ *                MSB-first canonical codes (src/huffman_codebook.py:126-226)
+ *
+ * Conventions
+ *   - Every pointer named *_dev is device memory; sizes are int64_t.
+ *   - `stream` is a cudaStream_t passed as void*; work is enqueued there and
+ *     the call returns without synchronising.
+ *   - Return value: CBQ_OK or a CBQ_ERR_* code (argument errors are detected
+ *     on the host before any launch).  Errors found while decoding (a code
+ *     that matches no symbol, a row that ends where the next does not start,
+ *     a wait that timed out) are recorded in the optional device status word
+ *     `status_dev` (uint32_t[4], see CBQ_STATUS_*), which the caller zeroes
+ *     and reads back when it chooses.  No kernel traps.
+ *   - dtype codes: CBQ_F32 or CBQ_BF16 for activations and outputs; the
+ *     codebook is always fp32 and accumulation is always fp32.
+ *   - Handles do not exist: callers own every buffer.  Buffers that the
+ *     kernels read past their logical end must be allocated with the sizes
+ *     the *_bytes() queries return (zero-filled padding) and be 16-byte
+ *     aligned.
+ *
+ * The functions replace the reference's GPU entry points (paths relative
+ * to the reference project root):
+ *   fused_compressed_linear     src/gpu_accelerated_functions.py:238-274
+ *   fused_compressed_embedding  src/gpu_accelerated_functions.py:276-307
+ *   huffman_decode_to_i32 + huffman_i32_linear
+ *                               src/gpu_huffman_functions.py:297-370
+ *   huffman_decode_to_i32 + huffman_i32_embedding
+ *                               src/gpu_huffman_functions.py:372-405
+ * and follow the status-code style of the reference's HIP C ABI
+ * (rocm/compressed_kernel.h:37-39, rocm/compressed_kernel.hip:607-616).
+ */
+#ifndef CBQ_H
+#define CBQ_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (rocm/compressed_kernel.h:37-39 has 0/1/2) ---- */
+#define CBQ_OK              0
+#define CBQ_ERR_CUDA        1   /* a CUDA runtime call failed */
+#define CBQ_ERR_ARG         2   /* invalid argument (checked on the host) */
+#define CBQ_ERR_CORRUPT     3   /* decode error recorded in a status word */
+#define CBQ_ERR_TIMEOUT     4   /* a bounded device wait gave up */
+#define CBQ_ERR_UNSUPPORTED 5   /* shape/format outside what the kernels accept */
+
+/* ---- device status word layout: uint32_t status_dev[4] ---- */
+#define CBQ_STATUS_FLAGS     0  /* OR of CBQ_FLAG_* */
+#define CBQ_STATUS_FIRST_ROW 1  /* smallest row index with an error (init 0xffffffff) */
+#define CBQ_STATUS_COUNT     2  /* number of decode errors */
+#define CBQ_FLAG_CORRUPT  1u    /* a Huffman code matched no symbol (reference emits symbol 0, advances 1 bit) */
+#define CBQ_FLAG_ROW_END  2u    /* a row's decoded end != next row's start */
+#define CBQ_FLAG_TIMEOUT  4u    /* an mbarrier wait exceeded its bound */
+#define CBQ_FLAG_SPAN     8u    /* a tile's stream span exceeded the staging buffer */
+
+/* ---- dtypes ---- */
+#define CBQ_F32  0
+#define CBQ_BF16 1
+
+const char *cbq_status_string(int status);
+int cbq_version(void);
+
+/* ======================================================================
+ * Fixed-width streams
+ * ====================================================================== */
+
+/* Device bytes to allocate for an M x K, `bits`-wide stream: the on-disk
+ * ceil(M*K*bits/8) bytes plus zero padding the kernels may read.  The
+ * reference pads +4 bytes on the GPU (src/gpu_accelerated_functions.py:860-864). */
+int64_t cbq_fixed_stream_bytes(int64_t M, int64_t K, int bits);
+
+/* out[t, r] = sum_k x[t, k] * codebook[min(idx(r*K + k), C-1)] (+ bias[r]).
+ * Replaces fused_compressed_linear (src/gpu_accelerated_functions.py:238-274)
+ * and ck_linear_f32 (rocm/compressed_kernel.hip:607-616).
+ *   x_dev      [T, ldx] rows of K activations, dtype x_dtype
+ *   packed_dev fixed-width stream, packed_bytes >= cbq_fixed_stream_bytes()
+ *   codebook_dev fp32[C], C >= 1;  bits in [1, 16]
+ *   bias_dev   fp32[M] or NULL
+ *   out_dev    [T, ldo] rows of M outputs, dtype out_dtype (overwritten) */
+int cbq_linear_fixed(const void *x_dev, int x_dtype, int64_t T, int64_t ldx,
+                     const uint8_t *packed_dev, int64_t packed_bytes,
+                     const float *codebook_dev, int64_t C, int bits,
+                     int64_t M, int64_t K, const float *bias_dev,
+                     void *out_dev, int out_dtype, int64_t ldo, void *stream);
+
+/* out[t, h] = codebook[min(idx(ids[t]*H + h), C-1)] for a [vocab, H] table.
+ * Replaces fused_compressed_embedding (src/gpu_accelerated_functions.py:276-307).
+ * Token ids outside [0, vocab) are an argument error detected on the device:
+ * their rows are zero-filled and CBQ_FLAG_CORRUPT is set in status_dev. */
+int cbq_embedding_fixed(const int64_t *ids_dev, int64_t T,
+                        const uint8_t *packed_dev, int64_t packed_bytes,
+                        const float *codebook_dev, int64_t C, int bits,
+                        int64_t vocab, int64_t H, void *out_dev, int out_dtype,
+                        uint32_t *status_dev, void *stream);
+
+/* Write the LSB-first stream of n indices (the device twin of
+ * pack_any_bits, src/bitpack.py:32-94).  out_bytes >= ceil(n*bits/8) rounded
+ * up to 4; bytes past ceil(n*bits/8) are written as zero. */
+int cbq_pack_fixed(const uint16_t *idx_dev, int64_t n, int bits,
+                   uint8_t *out_dev, int64_t out_bytes, void *stream);
+
+/* ======================================================================
+ * Canonical-Huffman streams
+ * ====================================================================== */
+
+/* Decode tables derived from huff_lengths (uint8[alphabet]); the CUDA kernels
+ * use these instead of the stored 12-bit tables, which carry the same codes
+ * (src/huffman_codebook.py:353-423).  Build on the host, copy to the device
+ * verbatim (the blob contains no pointers). */
+int64_t cbq_huff_tables_bytes(int64_t alphabet);
+int cbq_huff_tables_build(const uint8_t *huff_lengths, int64_t alphabet,
+                          void *tables_host, int64_t tables_bytes);
+/* Longest code length in a built table blob (0 = empty code). */
+int cbq_huff_tables_max_len(const void *tables_host);
+
+/* Device bytes to allocate for a Huffman stream whose on-disk `huff_stream`
+ * has stream_len bytes (it already ends with 4 zero bytes). */
+int64_t cbq_huff_stream_bytes(int64_t stream_len);
+
+/* Symbols per entry of the chunk-entry table, and its element count. */
+#define CBQ_HUFF_CHUNK 64
+int64_t cbq_huff_chunk_count(int64_t M, int64_t K);
+
+/* Load-time pass: decode every row once and record, for each row r and
+ * chunk c, the bit offset of symbol c*64 relative to row_bit_starts[r]
+ * (uint32_t chunk_dev[M * ceil(K/64)]).  The reference format has only
+ * per-row entry points (src/huffman_codebook.py:213); this table gives the
+ * GEMV 64-symbol entry points.  Records CBQ_FLAG_ROW_END when a row does
+ * not end where the next one starts and CBQ_FLAG_CORRUPT for undecodable
+ * codes, in status_dev. */
+int cbq_huff_chunk_table(const uint8_t *stream_dev, int64_t stream_bytes,
+                         const void *tables_dev, const int64_t *row_bit_starts_dev,
+                         int64_t M, int64_t K, int64_t total_bits,
+                         uint32_t *chunk_dev, uint32_t *status_dev, void *stream);
+
+/* Fused Huffman decode + GEMV: same result as cbq_linear_fixed on the
+ * decoded indices.  Replaces huffman_decode_to_i32 + huffman_i32_linear
+ * (src/gpu_huffman_functions.py:297-370), without the int32 [M,K] buffer.
+ * total_bits = 8 * (stream_len - 4): the end of the last row. */
+int cbq_linear_huff(const void *x_dev, int x_dtype, int64_t T, int64_t ldx,
+                    const uint8_t *stream_dev, int64_t stream_bytes,
+                    const void *tables_dev, const int64_t *row_bit_starts_dev,
+                    const uint32_t *chunk_dev, int64_t total_bits,
+                    const float *codebook_dev, int64_t C,
+                    int64_t M, int64_t K, const float *bias_dev,
+                    void *out_dev, int out_dtype, int64_t ldo,
+                    uint32_t *status_dev, void *stream);
+
+/* Huffman embedding: decodes only the requested rows (the reference decodes
+ * the whole table per call, src/gpu_huffman_functions.py:966-978). */
+int cbq_embedding_huff(const int64_t *ids_dev, int64_t T,
+                       const uint8_t *stream_dev, int64_t stream_bytes,
+                       const void *tables_dev, const int64_t *row_bit_starts_dev,
+                       const uint32_t *chunk_dev, const float *codebook_dev,
+                       int64_t C, int64_t vocab, int64_t H,
+                       void *out_dev, int out_dtype, uint32_t *status_dev,
+                       void *stream);
+
+/* Decode rows to uint16 indices (the device twin of
+ * huffman_decode_indices, src/huffman_codebook.py:259-340; used to check
+ * bit-exactness, not on the GEMV path). */
+int cbq_huff_decode_indices(const uint8_t *stream_dev, int64_t stream_bytes,
+                            const void *tables_dev, const int64_t *row_bit_starts_dev,
+                            const uint32_t *chunk_dev, int64_t M, int64_t K,
+                            uint16_t *idx_dev, uint32_t *status_dev, void *stream);
+
+/* Encode n indices with canonical codes (code_dev uint32[alphabet],
+ * len_dev uint8[alphabet]) at the given exclusive bit starts (int64[n]),
+ * MSB-first (the device twin of src/huffman_codebook.py:167-201).  out_dev
+ * must hold out_bytes >= ceil(total_bits/8) + 8 bytes; it is zeroed here. */
+int cbq_huff_encode(const uint16_t *idx_dev, int64_t n, const uint32_t *code_dev,
+                    const uint8_t *len_dev, const int64_t *bit_starts_dev,
+                    uint8_t *out_dev, int64_t out_bytes, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CBQ_H */
