@@ -1,9 +1,10 @@
-"""Benchmark: compressed decode throughput at Qwen3-8B shape, batch 1.
+"""Benchmark: compressed greedy decode throughput at Qwen3-8B shape, batch 1.
 
-One step = one decode token through every compressed matrix of a Qwen3-8B
-architecture model (36 layers x q,k,v,o,gate,up,down + lm_head; 12.3 GB of
-13-bit streams) at T=1 with bf16 activations, chained layer to layer, with an
-NCCL all-reduce after o_proj and down_proj when tensor-parallel (N > 1).
+One step = one greedy decode token of a Qwen3-8B-architecture model whose
+every matrix stays compressed (36 layers x q,k,v,o,gate,up,down + lm_head +
+embedding; 12.3 GB of 13-bit streams), bf16 activations, KV cache, the whole
+step replayed from one CUDA graph, with an NCCL all-reduce after o_proj and
+down_proj when tensor-parallel (N > 1).
 Weights are seeded synthetic bf16 N(0, 0.02) compressed losslessly on the GPU
 with one codebook per category.  The 12.3 GB of inputs is
 ~100x the 126 MB L2, so no flush is needed between steps.
@@ -47,7 +48,13 @@ def parse():
     ap.add_argument("--impl", default="cbq", choices=["cbq", "reference"])
     ap.add_argument("--huffman", action="store_true", help="Huffman-coded streams instead of fixed width")
     ap.add_argument("--model", default="qwen3-8b", choices=["qwen3-8b", "qwen3-1.7b"])
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--no-graph", action="store_true", help="eager steps instead of a CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="decode", choices=["decode", "gemv"],
+                    help="decode: Qwen3 greedy decode (headline); gemv: one matrix shape, GB/s")
+    ap.add_argument("--shape", default="12288,4096", help="gemv workload: M,K")
+    ap.add_argument("--tokens", type=int, default=1, help="gemv workload: T (activation rows)")
     return ap.parse_args()
 
 
@@ -179,54 +186,122 @@ def reference_arm(args):
 
 # ------------------------------------------------------------------ GPU arm
 
+def graph_time_ms(torch, fn, reps, dev):
+    """Average ms of fn() captured once in a CUDA graph and replayed reps times."""
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    g.replay()
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize(dev)
+    return a.elapsed_time(b) / reps
+
+
+def gemv_workload(args):
+    """One compressed matrix shape: R distinct seeded copies (> 2x L2 in total)
+    decode-GEMV'd in turn from a CUDA graph; reports GB/s over algorithmic bytes."""
+    import importlib
+    import torch
+    cbq = importlib.import_module(PKG)
+    dev = torch.device("cuda", 0)
+    M, K = (int(v) for v in args.shape.split(","))
+    T = args.tokens
+    comp = cbq.synth.GpuCompressor(dev)
+    per = (M * K * 13) // 8
+    R = max(2, min(64, (512 << 20) // max(per, 1) + 1))
+    mats, alg = [], 0
+    for r in range(R):
+        bits = cbq.synth.bf16_normal_gpu((M, K), seed=1000 + r, device=dev)
+        d = comp.compress(bits, huffman=args.huffman)
+        if args.huffman:
+            lin = cbq.HuffmanCodebookLinear("g", d["huff_stream"], d["huff_lengths"], int(d["huff_n"][0]),
+                                            d["codebook"], (M, K), d["bits"],
+                                            huff_row_bit_starts=d["huff_row_bit_starts"], device=dev)
+            b = lin.hs.compressed_bytes
+        else:
+            lin = cbq.GPUAcceleratedLinear("g", d["indices"], d["codebook"], (M, K), d["bits"], device=dev)
+            b = (M * K * d["bits"] + 7) // 8
+        alg += b + 4 * lin.C + 2 * K * T + 2 * M * T
+        mats.append(lin)
+        del bits, d
+    x = torch.randn(T, K, device=dev).to(torch.bfloat16)
+    outs = [torch.empty(T, M, device=dev, dtype=torch.bfloat16) for _ in mats]
+    for _ in range(args.warmup):
+        for m, o in zip(mats, outs):
+            m(x, out=o)
+    torch.cuda.synchronize()
+    with ClockSampler(0) as clk:
+        ms = graph_time_ms(torch, lambda: [m(x, out=o) for m, o in zip(mats, outs)], args.steps, dev)
+    us = ms * 1e3 / R
+    gbs = alg / R / (us * 1e-6) / 1e9
+    peak, peak_kind = measured_peaks()
+    kern = "k_linear_huff" if args.huffman else "k_linear_fixed"
+    line = {"metric": "compressed GEMV GB/s vs HBM", "value": gbs, "unit": "GB/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic seeded bf16 N(0,0.02), lossless per-matrix codebook",
+            "config": {"workload": f"{kern} {M}x{K} T={T} {'huffman' if args.huffman else 'fixed'}",
+                       "copies": R, "l2": f"{R} distinct matrices rotated (> 2x L2)",
+                       "bits": mats[0].bits},
+            "roofline": {"kernel": kern, "bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                         "frac": gbs / peak, "peak_kind": peak_kind, "traffic": None,
+                         "alg_bytes_per_launch": alg / R, "us_per_launch": us},
+            "gpu_launches": args.steps * R, "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return reference_arm(args)
+    if args.workload == "gemv":
+        return gemv_workload(args)
     import importlib
     import torch
     import torch.distributed as dist
     cbq = importlib.import_module(PKG)
     q3 = cbq.qwen3
+    from importlib import import_module
+    qd = import_module(PKG + ".qwen3_decode")
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    group = None
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=180))
+        group = dist.group.WORLD
     cfg = q3.QWEN3_8B if args.model == "qwen3-8b" else q3.QWEN3_1_7B
     t0 = time.time()
     W = q3.CompressedQwen3Weights(cfg, dev, huffman=args.huffman, rank=rank, world=world)
     setup_s = time.time() - t0
-    L = W.layers
-    names = [s.name for s in q3.linear_specs(cfg) if s.name != "model.embed_tokens.weight"]
     H = cfg.hidden
-
-    def allreduce(t):
-        if world > 1:
-            dist.all_reduce(t)
-        return t
-
-    def step(x):
-        """One token through the compressed linear stack (bf16, T=1)."""
-        for i in range(cfg.layers):
-            p = f"model.layers.{i}."
-            q = L[p + "self_attn.q_proj.weight"](x)
-            L[p + "self_attn.k_proj.weight"](x)
-            L[p + "self_attn.v_proj.weight"](x)
-            o = allreduce(L[p + "self_attn.o_proj.weight"](q))
-            x = torch.nn.functional.rms_norm(x + o, (H,))
-            g = L[p + "mlp.gate_proj.weight"](x)
-            u = L[p + "mlp.up_proj.weight"](x)
-            dn = allreduce(L[p + "mlp.down_proj.weight"](torch.nn.functional.silu(g) * u))
-            x = torch.nn.functional.rms_norm(x + dn, (H,))
-        return L["lm_head.weight"](x)
-
-    x0 = torch.randn(1, H, device=dev).to(torch.bfloat16)
-    for _ in range(args.warmup):
-        step(x0)
+    prompt_len = 64
+    max_len = prompt_len + args.warmup + 2 * args.steps + 8
+    dec = qd.Qwen3Decoder(W, batch=args.batch, max_len=max_len, act_dtype=torch.bfloat16, group=group)
+    g = torch.Generator().manual_seed(1234)
+    prompt = torch.randint(0, cfg.vocab, (args.batch, prompt_len), generator=g)
+    if not args.no_graph:
+        dec.capture()
+    dec.reset()
+    dec.generate(prompt, 1)                      # prompt fills the cache (untimed)
+    for _ in range(args.warmup):                 # greedy decode steps, untimed
+        dec.ids.copy_(dec.next_ids)
+        dec.run_step()
+        dec.pos.add_(1)
     torch.cuda.synchronize()
 
     def timed(fn, n):
@@ -246,33 +321,39 @@ def main():
             ms = float(t.item())
         return ms
 
-    with ClockSampler(local) as clk:
-        ms = timed(lambda: step(x0), args.steps)
-    ms_step = ms / args.steps
-    value = 1000.0 / ms_step
+    def decode_step():
+        dec.ids.copy_(dec.next_ids)
+        dec.run_step()
+        dec.pos.add_(1)
 
-    # end to end: pinned host input in, lm_head logits out, every step
-    x_host = x0.cpu().pin_memory()
-    out_host = torch.empty((1, cfg.vocab // world), dtype=torch.bfloat16).pin_memory()
+    with ClockSampler(local) as clk, torch.cuda.nvtx.range("cbq_timed"):
+        ms = timed(decode_step, args.steps)
+    ms_step = ms / args.steps
+    value = args.batch * 1000.0 / ms_step
+
+    # end to end: the token id goes host -> device and the next one device -> host every step
+    ids_host = dec.next_ids.cpu().pin_memory()
+    next_host = torch.empty_like(ids_host).pin_memory()
 
     def e2e_step():
-        xd = x_host.to(dev, non_blocking=True)
-        y = step(xd)
-        out_host.copy_(y, non_blocking=True)
-    for _ in range(2):
-        e2e_step()
+        dec.ids.copy_(ids_host, non_blocking=True)
+        dec.run_step()
+        dec.pos.add_(1)
+        next_host.copy_(dec.next_ids, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        ids_host.copy_(next_host)
     ms_e2e = timed(e2e_step, args.steps) / args.steps
+    dec.release()
 
-    # dominant kernel: gate_proj decode-GEMV over all layers' weights (2.9 GB > L2)
-    gates = [L[f"model.layers.{i}.mlp.gate_proj.weight"] for i in range(cfg.layers)]
-    xg = torch.randn(1, H, device=dev).to(torch.bfloat16)
-    reps = 5
-    for g in gates:
-        g(xg)
-    gms = timed(lambda: [g(xg) for g in gates], reps) / (reps * len(gates))
+    # dominant kernel: gate_proj decode-GEMV over all 36 layers' weights (graph-replayed)
+    gates = [W.layers[f"model.layers.{i}.mlp.gate_proj.weight"] for i in range(cfg.layers)]
+    xg = torch.randn(args.batch, H, device=dev).to(torch.bfloat16)
+    outs = [torch.empty(args.batch, gt.M, device=dev, dtype=torch.bfloat16) for gt in gates]
+    gms = graph_time_ms(torch, lambda: [gt(xg, out=o) for gt, o in zip(gates, outs)], 20, dev) / len(gates)
     g0 = gates[0]
-    alg = W.stream_bytes["model.layers.0.mlp.gate_proj.weight"] + 4 * W.codebooks["mlp_ffn"].numel() \
-        + 2 * H + 2 * g0.M
+    cbn = W.codebooks["mlp_ffn"].numel()
+    alg = W.stream_bytes["model.layers.0.mlp.gate_proj.weight"] + 4 * cbn + 2 * H * args.batch \
+        + 2 * g0.M * args.batch
     peak, peak_kind = measured_peaks()
     achieved = alg / (gms * 1e-3) / 1e9
 
@@ -285,29 +366,31 @@ def main():
         cpu = {"value": 1.0 / float(np.mean(secs)), "unit": "tok/s", "cores": oracle.threads(),
                "kind": kind, "sample": desc}
 
-    launches = args.steps * (len(names))
+    n_lin = len([s for s in q3.linear_specs(cfg)])          # embedding + 7 per layer + lm_head
     stack_bytes = W.total_stream_bytes()
     if rank == 0:
         line = {
             "metric": "compressed decode tok/s (Qwen3-8B shape, bs1)", "value": value, "unit": "tok/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded bf16 N(0,0.02) weights, lossless per-category codebooks)",
-            "config": {"workload": f"{cfg.name} decode linear stack (36 layers x 7 GEMVs + lm_head), bs1, "
-                                   f"{'huffman' if args.huffman else 'fixed 13-bit'}",
-                       "global_batch": 1, "parallelism": f"tp{world}",
-                       "l2": "inputs 12.3 GB >> 126 MB L2 (no flush)",
+            "data": "synthetic (seeded bf16 N(0,0.02) weights, lossless per-category codebooks, "
+                    "64 seeded prompt tokens)",
+            "config": {"workload": f"{cfg.name} greedy decode, batch {args.batch}, "
+                                   f"{'huffman' if args.huffman else 'fixed 13-bit'} streams, CUDA graph",
+                       "global_batch": args.batch, "seq_len": max_len, "parallelism": f"tp{world}",
+                       "l2": "weights 12.3 GB >> 126 MB L2 (no flush)",
                        "stream_bytes_per_rank": stack_bytes,
                        "hbm_gbs_whole_step": stack_bytes / (ms_step * 1e-3) / 1e9,
                        "setup_s": round(setup_s, 1)},
-            "roofline": {"kernel": "k_linear_fixed<13,1,bf16,bf16> (gate_proj 12288x4096)" if not args.huffman
-                         else "k_linear_huff<1,bf16,bf16> (gate_proj)",
+            "roofline": {"kernel": ("k_linear_huff" if args.huffman else "k_linear_fixed<13,1,bf16,bf16>")
+                                   + f" gate_proj {g0.M}x{g0.K}",
                          "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
-                         "alg_bytes_per_launch": alg, "us_per_launch": gms * 1e3},
-            "e2e": {"value": 1000.0 / ms_e2e, "unit": "tok/s", "h2d_bytes_per_step": 2 * H,
-                    "d2h_bytes_per_step": 2 * (cfg.vocab // world)},
-            "gpu_launches": launches,
+                         "alg_bytes_per_launch": alg, "us_per_launch": gms * 1e3,
+                         "timing": "CUDA-graph replay of the 36 gate_proj launches, CUDA events"},
+            "e2e": {"value": args.batch * 1000.0 / ms_e2e, "unit": "tok/s",
+                    "h2d_bytes_per_step": 8 * args.batch, "d2h_bytes_per_step": 8 * args.batch},
+            "gpu_launches": args.steps * n_lin,
             "clocks": clk.summary(),
         }
         if cpu:

@@ -12,6 +12,8 @@ namespace cbq {
 constexpr int kThreads = 256;            // threads per CTA of the GEMV kernels
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s bound on any device-side wait
 
+__host__ __device__ constexpr size_t a128(size_t v) { return (v + 127) & ~(size_t)127; }
+
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

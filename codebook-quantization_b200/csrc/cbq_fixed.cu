@@ -101,14 +101,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_linear_fixed(const FixedArgs a)
     const int RB = a.RB, nst = a.nst;
     const int tile_chunks = RB * kc;
 
+    // Every region starts on a 128-byte boundary (the bulk-copy destination
+    // needs 16, the float4 loads of x need 16); fixed_smem() mirrors this.
     uint64_t *bar = reinterpret_cast<uint64_t *>(smem);
     size_t off = 128;
     float *cb_s = reinterpret_cast<float *>(smem + off);
-    off += ((size_t)a.C * 4 + 15) & ~(size_t)15;
+    off += a128((size_t)a.C * 4);
     float *xs = reinterpret_cast<float *>(smem + off);
-    off += (size_t)TB * XS * 4;
+    off += a128((size_t)TB * XS * 4);
     float *P = reinterpret_cast<float *>(smem + off);
-    off += ((size_t)TB * tile_chunks * 4 + 127) & ~(size_t)127;
+    off += a128((size_t)TB * tile_chunks * 4);
     uint8_t *stg = smem + off;
 
     if (tid == 0) {
@@ -287,9 +289,9 @@ struct FixedPlan {
 size_t fixed_smem(int C, int K, int RB, int TB, int nst, uint32_t stage_bytes) {
     const int kc = K / 32;
     size_t s = 128;
-    s += ((size_t)C * 4 + 15) & ~(size_t)15;
-    s += (size_t)TB * kc * 36 * 4;
-    s += ((size_t)TB * RB * kc * 4 + 127) & ~(size_t)127;
+    s += a128((size_t)C * 4);
+    s += a128((size_t)TB * kc * 36 * 4);
+    s += a128((size_t)TB * RB * kc * 4);
     s += (size_t)nst * stage_bytes;
     return s;
 }

@@ -21,6 +21,7 @@
 // padding word per 64 so that neighbouring chunks hit distinct banks).  Chunk
 // sums are reduced per row by one warp in fixed order (deterministic).
 #include <algorithm>
+#include <cstddef>
 #include <cstring>
 #include <mutex>
 #include <numeric>
@@ -48,18 +49,21 @@ struct HuffTables {
     uint64_t limit[kMaxLen + 1];   // first[L] + count[L]: one past the last length-L code
     uint64_t first[kMaxLen + 1];   // first canonical code of length L
     int32_t offset[kMaxLen + 1];   // index in syms[] of the first length-L symbol
-    int32_t pad_;
+    int32_t pad_[3];               // puts lut on a 16-byte boundary (read with 16-byte loads)
     uint32_t lut[kLutSize];        // (len << 16) | sym for codes <= 12 bits; 0 otherwise
     // uint16_t syms[n_used] follows: symbols in (length, code) order
 };
-static_assert(sizeof(HuffTables) % 8 == 0, "blob alignment");
+static_assert(offsetof(HuffTables, lut) % 16 == 0, "lut must be 16-byte aligned for uint4 loads");
+static_assert(offsetof(HuffTables, lut) == 688, "blob layout is part of the ABI (tests decode it)");
+static_assert(sizeof(HuffTables) % 16 == 0, "blob alignment");
 
 __host__ __device__ inline const uint16_t *blob_syms(const HuffTables *t) {
     return reinterpret_cast<const uint16_t *>(t + 1);
 }
 
 // Shared-memory copy of the parts of the tables every symbol may touch.
-struct SmemTables {
+// 16-byte aligned: load_tables() fills lut with 16-byte stores.
+struct alignas(16) SmemTables {
     uint32_t lut[kLutSize];
     uint64_t limit[kMaxLen + 1];
     uint64_t first[kMaxLen + 1];
@@ -230,17 +234,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_linear_huff(const HuffArgs a) {
     const int RB = a.RB, nst = a.nst;
     const int tile_chunks = RB * nch;
 
+    // Every region starts on a 128-byte boundary (the bulk-copy destination
+    // needs 16); huff_smem() on the host mirrors this carve-up exactly.
     uint64_t *bar = reinterpret_cast<uint64_t *>(smem);
     int64_t *b0s = reinterpret_cast<int64_t *>(smem + 128);
     size_t off = 256;
     SmemTables *st = reinterpret_cast<SmemTables *>(smem + off);
-    off += (sizeof(SmemTables) + 15) & ~(size_t)15;
+    off += a128(sizeof(SmemTables));
     float *cb_s = reinterpret_cast<float *>(smem + off);
-    if (CBS) off += ((size_t)a.C * 4 + 15) & ~(size_t)15;
+    if (CBS) off += a128((size_t)a.C * 4);
     float *xs = reinterpret_cast<float *>(smem + off);
-    off += (size_t)TB * XSH * 4;
+    off += a128((size_t)TB * XSH * 4);
     float *P = reinterpret_cast<float *>(smem + off);
-    off += ((size_t)TB * tile_chunks * 4 + 127) & ~(size_t)127;
+    off += a128((size_t)TB * tile_chunks * 4);
     uint8_t *stg = smem + off;
 
     if (tid == 0) {
@@ -437,10 +443,10 @@ struct HuffPlan {
 
 size_t huff_smem(int C, bool cbs, int K, int RB, int TB, int nst, uint32_t cap) {
     const int nch = (K + S - 1) / S;
-    size_t s = 256 + ((sizeof(SmemTables) + 15) & ~(size_t)15);
-    if (cbs) s += ((size_t)C * 4 + 15) & ~(size_t)15;
-    s += (size_t)TB * nch * (S + 1) * 4;
-    s += ((size_t)TB * RB * nch * 4 + 127) & ~(size_t)127;
+    size_t s = 256 + a128(sizeof(SmemTables));
+    if (cbs) s += a128((size_t)C * 4);
+    s += a128((size_t)TB * nch * (S + 1) * 4);
+    s += a128((size_t)TB * RB * nch * 4);
     s += (size_t)nst * cap;
     return s;
 }

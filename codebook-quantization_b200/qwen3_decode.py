@@ -1,0 +1,184 @@
+"""Greedy decode of a compressed Qwen3-architecture model on the GPU.
+
+The math is HF ``Qwen3ForCausalLM``'s (transformers ``models/qwen3``): RMSNorm
+in fp32 then cast back, q/k per-head RMSNorm before rotary embedding
+(rotate-half form, inv_freq = theta^(-2i/d)), grouped-query attention with
+softmax scaling d^-1/2, SiLU-gated MLP, residual adds in the activation dtype,
+final RMSNorm and lm_head, greedy argmax (first index on ties).  Every linear
+and the embedding run on ``libcbq``'s kernels; norms have unit weights (the
+synthetic models keep them exact at 1.0).
+
+Decode is one token per sequence per step.  The step reads the token ids and
+the position from static device buffers, writes the new key/value rows into a
+static cache and attends over it with a position mask, so it is captured once
+in a CUDA graph and replayed for every prompt and generated token with no host
+synchronisation.  Under tensor parallelism (``group`` given) heads and MLP
+columns are split per rank, o_proj/down_proj partial sums are all-reduced over
+NCCL, and the greedy argmax combines each rank's (max, index) pair.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+from .qwen3 import CompressedQwen3Weights
+
+__all__ = ["Qwen3Decoder", "rope_tables"]
+
+
+def rope_tables(head_dim: int, max_len: int, theta: float, device):
+    """cos/sin [max_len, head_dim] in fp32, HF's default rotary layout,
+    computed on the host (as HF does on a CPU model) and copied to ``device``."""
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.int64).float() / head_dim))
+    t = torch.arange(max_len, dtype=torch.float32)
+    f = (inv[:, None] @ t[None, :]).T
+    emb = torch.cat((f, f), dim=-1)
+    return emb.cos().to(device), emb.sin().to(device)
+
+
+def _rotate_half(x):
+    h = x.shape[-1] // 2
+    return torch.cat((-x[..., h:], x[..., :h]), dim=-1)
+
+
+def _rms(x, eps):
+    dt = x.dtype
+    x32 = x.float()
+    x32 = x32 * torch.rsqrt(x32.pow(2).mean(-1, keepdim=True) + eps)
+    return x32.to(dt)
+
+
+class Qwen3Decoder:
+    def __init__(self, weights: CompressedQwen3Weights, batch: int, max_len: int,
+                 act_dtype=torch.bfloat16, group: Optional[dist.ProcessGroup] = None):
+        self.w, self.cfg = weights, weights.cfg
+        cfg = self.cfg
+        self.dev = weights.device
+        self.B, self.max_len, self.dt = batch, max_len, act_dtype
+        self.group = group
+        self.world = weights.world
+        self.rank = weights.rank
+        self.hl = cfg.heads // self.world
+        self.kvl = cfg.kv_heads // self.world
+        if self.hl * self.world != cfg.heads or self.kvl * self.world != cfg.kv_heads:
+            raise ValueError(f"heads {cfg.heads}/{cfg.kv_heads} do not split over {self.world} ranks")
+        d = cfg.head_dim
+        self.cos, self.sin = rope_tables(d, max_len, cfg.rope_theta, self.dev)
+        self.k_cache = [torch.zeros(batch, self.kvl, max_len, d, dtype=act_dtype, device=self.dev)
+                        for _ in range(cfg.layers)]
+        self.v_cache = [torch.zeros_like(self.k_cache[0]) for _ in range(cfg.layers)]
+        self.ids = torch.zeros(batch, dtype=torch.int64, device=self.dev)
+        self.pos = torch.zeros(1, dtype=torch.int64, device=self.dev)
+        self.next_ids = torch.zeros(batch, dtype=torch.int64, device=self.dev)
+        self.logits = None
+        self.graph = None
+        self.vocab_local = cfg.vocab // self.world
+        self.ar = torch.arange(max_len, device=self.dev)
+        L = weights.layers
+        self.emb = L["model.embed_tokens.weight"]
+        self.lm_head = L["lm_head.weight"]
+        self.layer_mods = []
+        for i in range(cfg.layers):
+            p = f"model.layers.{i}."
+            self.layer_mods.append(tuple(L[p + n + ".weight"] for n in (
+                "self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "self_attn.o_proj",
+                "mlp.gate_proj", "mlp.up_proj", "mlp.down_proj")))
+
+    # --------------------------------------------------------------- one step
+    def _allreduce(self, t):
+        if self.world > 1:
+            dist.all_reduce(t, group=self.group)
+        return t
+
+    def _step(self):
+        cfg, B, d, eps, dt = self.cfg, self.B, self.cfg.head_dim, self.cfg.rms_eps, self.dt
+        x = self.emb(self.ids, out_dtype=dt)                         # [B, H]
+        cos = self.cos.index_select(0, self.pos).to(dt)              # [1, d]
+        sin = self.sin.index_select(0, self.pos).to(dt)
+        mask = (self.ar <= self.pos).view(1, 1, 1, self.max_len)
+        for li, (q_p, k_p, v_p, o_p, g_p, u_p, d_p) in enumerate(self.layer_mods):
+            h = _rms(x, eps)
+            q = _rms(q_p(h).view(B, self.hl, d), eps)
+            k = _rms(k_p(h).view(B, self.kvl, d), eps)
+            v = v_p(h).view(B, self.kvl, d)
+            q = q * cos + _rotate_half(q) * sin
+            k = k * cos + _rotate_half(k) * sin
+            self.k_cache[li].index_copy_(2, self.pos, k.unsqueeze(2))
+            self.v_cache[li].index_copy_(2, self.pos, v.unsqueeze(2))
+            a = F.scaled_dot_product_attention(q.unsqueeze(2), self.k_cache[li], self.v_cache[li],
+                                               attn_mask=mask, scale=d ** -0.5, enable_gqa=True)
+            x = x + self._allreduce(o_p(a.reshape(B, self.hl * d)))
+            h = _rms(x, eps)
+            x = x + self._allreduce(d_p(F.silu(g_p(h)) * u_p(h)))
+        logits = self.lm_head(_rms(x, eps))                          # [B, V / world]
+        self.logits = logits
+        val, idx = logits.float().max(dim=-1)
+        idx = idx + self.rank * self.vocab_local
+        if self.world > 1:
+            vals = [torch.empty_like(val) for _ in range(self.world)]
+            idxs = [torch.empty_like(idx) for _ in range(self.world)]
+            dist.all_gather(vals, val, group=self.group)
+            dist.all_gather(idxs, idx, group=self.group)
+            best = torch.stack(vals).max(dim=0).indices              # first rank on ties
+            idx = torch.stack(idxs).gather(0, best.unsqueeze(0)).squeeze(0)
+        self.next_ids.copy_(idx)
+
+    def step(self, ids: torch.Tensor, pos: int) -> torch.Tensor:
+        """Eager step (no graph): returns the greedy next ids [B]."""
+        self.ids.copy_(ids)
+        self.pos.fill_(pos)
+        self._step()
+        return self.next_ids
+
+    def capture(self, warmup: int = 2) -> None:
+        """Warm up then capture one step in a CUDA graph."""
+        s = torch.cuda.Stream(self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(s):
+            for _ in range(warmup):
+                self._step()
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        torch.cuda.synchronize(self.dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._step()
+        torch.cuda.synchronize(self.dev)
+
+    def release(self) -> None:
+        """Drop the graph (before destroying an NCCL process group)."""
+        self.graph = None
+        torch.cuda.synchronize(self.dev)
+
+    def reset(self) -> None:
+        for k, v in zip(self.k_cache, self.v_cache):
+            k.zero_()
+            v.zero_()
+
+    def run_step(self) -> None:
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._step()
+
+    def generate(self, prompt: torch.Tensor, n_new: int) -> torch.Tensor:
+        """Greedy tokens [B, n_new] after the prompt [B, S] (fed one token per step)."""
+        B, S = prompt.shape
+        if S + n_new > self.max_len:
+            raise ValueError("sequence longer than the cache")
+        prompt = prompt.to(self.dev)
+        out = torch.empty(B, n_new, dtype=torch.int64, device=self.dev)
+        self.pos.zero_()
+        for t in range(S):
+            self.ids.copy_(prompt[:, t])
+            self.run_step()
+            self.pos.add_(1)
+        for t in range(n_new):
+            out[:, t].copy_(self.next_ids)
+            self.ids.copy_(self.next_ids)
+            if t + 1 < n_new:
+                self.run_step()
+                self.pos.add_(1)
+        return out

@@ -72,9 +72,9 @@ def _blob_view(blob):
     limit = np.frombuffer(blob[16:16 + 264].tobytes(), dtype=np.uint64)
     first = np.frombuffer(blob[280:280 + 264].tobytes(), dtype=np.uint64)
     offset = np.frombuffer(blob[544:544 + 132].tobytes(), dtype=np.int32)
-    lut = np.frombuffer(blob[680:680 + 16384].tobytes(), dtype=np.uint32)
+    lut = np.frombuffer(blob[688:688 + 16384].tobytes(), dtype=np.uint32)
     n_used = int(hdr[3])
-    syms = np.frombuffer(blob[17064:17064 + 2 * n_used].tobytes(), dtype=np.uint16)
+    syms = np.frombuffer(blob[17072:17072 + 2 * n_used].tobytes(), dtype=np.uint16)
     return hdr, limit, first, offset, lut, syms
 
 
