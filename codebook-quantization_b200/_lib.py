@@ -29,8 +29,9 @@ SIGNATURES = {
     "cbq_status_string": (ct.c_char_p, [_INT]),
     "cbq_version": (_INT, []),
     "cbq_fixed_stream_bytes": (_I64, [_I64, _I64, _INT]),
+    "cbq_linear_fixed_workspace_bytes": (_I64, [_I64, _I64, _I64]),
     "cbq_linear_fixed": (_INT, [_P, _INT, _I64, _I64, _P, _I64, _P, _I64, _INT, _I64, _I64, _P, _P,
-                                _INT, _I64, _P]),
+                                _INT, _I64, _P, _I64, _P]),
     "cbq_embedding_fixed": (_INT, [_P, _I64, _P, _I64, _P, _I64, _INT, _I64, _I64, _P, _INT, _P, _P]),
     "cbq_pack_fixed": (_INT, [_P, _I64, _INT, _P, _I64, _P]),
     "cbq_huff_tables_bytes": (_I64, [_I64]),
@@ -39,8 +40,11 @@ SIGNATURES = {
     "cbq_huff_stream_bytes": (_I64, [_I64]),
     "cbq_huff_chunk_count": (_I64, [_I64, _I64]),
     "cbq_huff_chunk_table": (_INT, [_P, _I64, _P, _P, _I64, _I64, _I64, _P, _P, _P]),
-    "cbq_linear_huff": (_INT, [_P, _INT, _I64, _I64, _P, _I64, _P, _P, _P, _I64, _P, _I64, _I64, _I64,
-                               _P, _P, _INT, _I64, _P, _P]),
+    "cbq_huff_decode_lut_bytes": (_I64, []),
+    "cbq_huff_build_decode_lut": (_INT, [_P, _P, _I64, _P, _P]),
+    "cbq_linear_huff_workspace_bytes": (_I64, [_I64, _I64, _I64]),
+    "cbq_linear_huff": (_INT, [_P, _INT, _I64, _I64, _P, _I64, _P, _P, _P, _P, _I64, _P, _I64, _I64,
+                               _I64, _P, _P, _INT, _I64, _P, _I64, _P, _P]),
     "cbq_embedding_huff": (_INT, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I64, _I64, _I64, _P, _INT, _P,
                                   _P]),
     "cbq_huff_decode_indices": (_INT, [_P, _I64, _P, _P, _P, _I64, _I64, _P, _P, _P]),

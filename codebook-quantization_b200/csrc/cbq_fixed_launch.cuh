@@ -1,0 +1,53 @@
+// cbq_fixed_launch.cuh -- per-width launchers of k_linear_fixed, explicitly
+// instantiated in cbq_fixed_w*.cu (split so the variants compile in parallel).
+#pragma once
+#include <mutex>
+
+#include "cbq_fixed_kernel.cuh"
+
+namespace cbq {
+
+template <int BITS, int TB, typename XT>
+int launch_fixed_one(const FixedArgs &a, size_t smem, int grid, cudaStream_t s) {
+    auto kern = k_linear_fixed<BITS, TB, XT>;
+    static std::mutex mu;
+    static size_t configured[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return CBQ_ERR_CUDA;
+    {
+        std::lock_guard<std::mutex> g(mu);
+        if (configured[dev & 63] < smem) {
+            if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+                cudaSuccess)
+                return CBQ_ERR_CUDA;
+            configured[dev & 63] = smem;
+        }
+    }
+    kern<<<grid, kFxWarps * 32, smem, s>>>(a);
+    return cudaGetLastError() == cudaSuccess ? CBQ_OK : CBQ_ERR_CUDA;
+}
+
+template <int BITS>
+int launch_fixed_bits(int TB, bool x_bf16, const FixedArgs &a, size_t smem, int grid, cudaStream_t s) {
+    if (x_bf16) {
+        switch (TB) {
+            case 1: return launch_fixed_one<BITS, 1, __nv_bfloat16>(a, smem, grid, s);
+            case 2: return launch_fixed_one<BITS, 2, __nv_bfloat16>(a, smem, grid, s);
+            case 4: return launch_fixed_one<BITS, 4, __nv_bfloat16>(a, smem, grid, s);
+            case 8: return launch_fixed_one<BITS, 8, __nv_bfloat16>(a, smem, grid, s);
+        }
+    } else {
+        switch (TB) {
+            case 1: return launch_fixed_one<BITS, 1, float>(a, smem, grid, s);
+            case 2: return launch_fixed_one<BITS, 2, float>(a, smem, grid, s);
+            case 4: return launch_fixed_one<BITS, 4, float>(a, smem, grid, s);
+            case 8: return launch_fixed_one<BITS, 8, float>(a, smem, grid, s);
+        }
+    }
+    return CBQ_ERR_UNSUPPORTED;
+}
+
+#define CBQ_INSTANTIATE_FIXED(B)                                                              \
+    template int launch_fixed_bits<B>(int, bool, const FixedArgs &, size_t, int, cudaStream_t);
+
+}  // namespace cbq

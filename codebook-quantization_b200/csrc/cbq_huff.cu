@@ -12,21 +12,16 @@
 //
 // GEMV (cbq_linear_huff): the reference format can only be entered at row
 // starts, so a load-time pass (cbq_huff_chunk_table) records the bit offset of
-// every 64th symbol of every row.  The GEMV then gives each thread one
-// 64-symbol chunk: a persistent CTA stages a tile of RB rows (one contiguous
-// bit range) into shared memory with cp.async.bulk, every thread decodes its
-// chunk from a 64-bit MSB-first bit buffer fed by 32-bit shared loads, looks
-// each code up in a shared 4096-entry table, gathers the fp32 codebook value
-// from shared memory and accumulates against x (fp32 in shared memory, one
-// padding word per 64 so that neighbouring chunks hit distinct banks).  Chunk
-// sums are reduced per row by one warp in fixed order (deterministic).
+// every 64th symbol of every row; a second load-time pass
+// (cbq_huff_build_decode_lut) folds the codebook into a two-level decode
+// table.  The fused kernel itself is in cbq_huff_kernel.cuh.
 #include <algorithm>
 #include <cstddef>
 #include <cstring>
 #include <mutex>
 #include <numeric>
 
-#include "cbq_common.cuh"
+#include "cbq_huff_kernel.cuh"
 
 namespace {
 
@@ -37,29 +32,10 @@ constexpr int kLutBits = 12;
 constexpr int kLutSize = 1 << kLutBits;
 constexpr int kMaxLen = 32;
 constexpr int S = CBQ_HUFF_CHUNK;          // symbols per chunk entry
-constexpr int kMaxCbSmem = 16384;
-constexpr int kMaxStages = 8;
 
-// Host/device table blob (no pointers; copied verbatim to the device).
-struct HuffTables {
-    uint32_t magic;
-    int32_t alphabet;
-    int32_t max_len;
-    int32_t n_used;
-    uint64_t limit[kMaxLen + 1];   // first[L] + count[L]: one past the last length-L code
-    uint64_t first[kMaxLen + 1];   // first canonical code of length L
-    int32_t offset[kMaxLen + 1];   // index in syms[] of the first length-L symbol
-    int32_t pad_[3];               // puts lut on a 16-byte boundary (read with 16-byte loads)
-    uint32_t lut[kLutSize];        // (len << 16) | sym for codes <= 12 bits; 0 otherwise
-    // uint16_t syms[n_used] follows: symbols in (length, code) order
-};
 static_assert(offsetof(HuffTables, lut) % 16 == 0, "lut must be 16-byte aligned for uint4 loads");
 static_assert(offsetof(HuffTables, lut) == 688, "blob layout is part of the ABI (tests decode it)");
 static_assert(sizeof(HuffTables) % 16 == 0, "blob alignment");
-
-__host__ __device__ inline const uint16_t *blob_syms(const HuffTables *t) {
-    return reinterpret_cast<const uint16_t *>(t + 1);
-}
 
 // Shared-memory copy of the parts of the tables every symbol may touch.
 // 16-byte aligned: load_tables() fills lut with 16-byte stores.
@@ -82,41 +58,6 @@ __device__ void load_tables(SmemTables *st, const HuffTables *g) {
     }
     if (threadIdx.x == 0) st->max_len = g->max_len;
 }
-
-__device__ __forceinline__ uint32_t bswap32(uint32_t v) { return __byte_perm(v, 0, 0x0123); }
-
-// 64-bit MSB-first bit buffer over 32-bit words of a byte stream.
-// Invariant before each decode: nb >= 32 valid bits at the top of buf.
-// Words at index >= nw read as zero, so a corrupt offset or stream can never
-// read outside the buffer it was given.
-struct BitBuf {
-    const uint32_t *w;
-    uint64_t wp;
-    uint64_t nw;
-    uint64_t buf;
-    int nb;
-    __device__ __forceinline__ uint32_t word(uint64_t i) const {
-        return (i < nw) ? bswap32(w[i]) : 0u;
-    }
-    __device__ __forceinline__ void init(const uint32_t *base, uint64_t nwords, uint64_t pos) {
-        w = base;
-        nw = nwords;
-        wp = pos >> 5;
-        const int sk = (int)(pos & 31);
-        const uint64_t v = ((uint64_t)word(wp) << 32) | word(wp + 1);
-        buf = v << sk;
-        nb = 64 - sk;
-        wp += 2;
-    }
-    __device__ __forceinline__ void consume(int n) {
-        buf <<= n;
-        nb -= n;
-        if (nb < 32) {
-            buf |= (uint64_t)word(wp++) << (32 - nb);
-            nb += 32;
-        }
-    }
-};
 
 // Decode the symbol at the top of `buf`; len = 0 means no code matched.
 __device__ __forceinline__ uint32_t decode_sym(uint64_t buf, const SmemTables *st,
@@ -176,178 +117,98 @@ __global__ void __launch_bounds__(128) k_huff_chunks(const uint8_t *stream, uint
     if (!end_ok || overflow) report(status, CBQ_FLAG_ROW_END, (uint32_t)r);
 }
 
-// ---------------------------------------------------------------- fused GEMV
+// ---------------------------------------------------------------- decode table
 
-struct HuffArgs {
-    const void *x;
-    int64_t ldx;
-    int64_t t0;
-    int ntok;
-    const uint8_t *stream;
-    int64_t stream_bytes;
-    const HuffTables *tables;
-    const int64_t *rbs;
-    const uint32_t *chunk;
-    int64_t total_bits;
-    const float *codebook;
-    int C;
-    int M, K;
-    const float *bias;
-    void *out;
-    int64_t ldo;
-    int RB, ntiles, nst;
-    uint32_t stage_cap;
-    uint32_t *status;
-};
-
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+// Length of the canonical code that starts the 32-bit window w (0: none).
+__device__ __forceinline__ int code_len_at(const HuffTables *t, uint32_t w, uint32_t &sym) {
+    for (int L = 1; L <= t->max_len; ++L) {
+        const uint64_t v = (uint64_t)(w >> (32 - L));
+        if (v < t->limit[L]) {
+            sym = blob_syms(t)[t->offset[L] + (uint32_t)(v - t->first[L])];
+            return L;
+        }
+    }
+    sym = 0;
+    return 0;
 }
 
-template <int TB, bool CBS>
-__device__ __forceinline__ void huff_chunk_dot(const uint32_t *words, uint64_t nwords, uint64_t pos,
-                                               int nsym,
-                                               const SmemTables *st, const uint16_t *gsyms,
-                                               const float *cb, uint32_t cmax, const float *xq,
-                                               int XSH, float (&acc)[TB], uint32_t &bad) {
-    BitBuf bb;
-    bb.init(words, nwords, pos);
-#pragma unroll 4
-    for (int i = 0; i < nsym; ++i) {
-        int len;
-        uint32_t sym = decode_sym(bb.buf, st, gsyms, len);
-        if (len == 0) { len = 1; ++bad; }
-        bb.consume(len);
-        const float wt = CBS ? cb[min(sym, cmax)] : __ldg(cb + min(sym, cmax));
-#pragma unroll
-        for (int t = 0; t < TB; ++t) acc[t] = fmaf(xq[t * XSH + i], wt, acc[t]);
+// One block of 1024 threads builds the two-level decode table
+// (layout in cbq_huff_kernel.cuh).  Thread i owns the 16 consecutive 14-bit
+// prefixes [16i, 16i+16); second-level tables are laid out in prefix order by
+// a block-wide exclusive scan and dropped (canonical search) once they would
+// exceed kHfSubMax entries.
+__global__ void __launch_bounds__(1024) k_huff_build_lut(const HuffTables *tab, const float *cb, int C,
+                                                         uint32_t *lut) {
+    __shared__ uint32_t warp_tot[32];
+    int exact = 1;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) exact &= (__float_as_uint(cb[c]) & 0xffffu) == 0;
+    exact = __syncthreads_and(exact);
+    auto payload = [&](uint32_t sym) -> uint32_t {
+        return exact ? (__float_as_uint(cb[min((int)sym, C - 1)]) >> 16) : sym;
+    };
+    constexpr int kPer = kHfLutSize / 1024;
+    const int p0 = threadIdx.x * kPer;
+    uint8_t depth[kPer];
+    uint32_t mine = 0;
+    for (int j = 0; j < kPer; ++j) {
+        const uint32_t p = (uint32_t)(p0 + j);
+        uint32_t sym;
+        const int L0 = code_len_at(tab, p << (32 - kHfLutBits), sym);
+        depth[j] = 0;
+        if (L0 >= 1 && L0 <= kHfLutBits) {
+            lut[p] = (payload(sym) << 16) | (uint32_t)L0;
+        } else if (L0 > kHfLutBits) {
+            uint32_t s2;
+            int L1 = code_len_at(tab, (p << (32 - kHfLutBits)) | ((1u << (32 - kHfLutBits)) - 1u), s2);
+            if (L1 == 0) L1 = 32;                           // incomplete code: cover every bit
+            depth[j] = (uint8_t)(L1 - kHfLutBits);
+            mine += 1u << depth[j];
+            lut[p] = 0;
+        } else {
+            lut[p] = 0;
+        }
     }
-}
-
-template <int TB, bool CBS, typename XT, typename OT>
-__global__ void __launch_bounds__(kThreads, 1) k_linear_huff(const HuffArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    const int tid = threadIdx.x;
-    const int K = a.K;
-    const int nch = (K + S - 1) / S;
-    const int XSH = nch * (S + 1);
-    const int RB = a.RB, nst = a.nst;
-    const int tile_chunks = RB * nch;
-
-    // Every region starts on a 128-byte boundary (the bulk-copy destination
-    // needs 16); huff_smem() on the host mirrors this carve-up exactly.
-    uint64_t *bar = reinterpret_cast<uint64_t *>(smem);
-    int64_t *b0s = reinterpret_cast<int64_t *>(smem + 128);
-    size_t off = 256;
-    SmemTables *st = reinterpret_cast<SmemTables *>(smem + off);
-    off += a128(sizeof(SmemTables));
-    float *cb_s = reinterpret_cast<float *>(smem + off);
-    if (CBS) off += a128((size_t)a.C * 4);
-    float *xs = reinterpret_cast<float *>(smem + off);
-    off += a128((size_t)TB * XSH * 4);
-    float *P = reinterpret_cast<float *>(smem + off);
-    off += a128((size_t)TB * tile_chunks * 4);
-    uint8_t *stg = smem + off;
-
-    if (tid == 0) {
-        for (int s = 0; s < nst; ++s) mbar_init(&bar[s], 1);
-        mbar_fence_init();
+    // block exclusive scan of `mine`
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t incl = mine;
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
     }
-    load_tables(st, a.tables);
-    if (CBS)
-        for (int i = tid; i < a.C; i += kThreads) cb_s[i] = a.codebook[i];
-    const XT *x = static_cast<const XT *>(a.x);
-    for (int i = tid; i < TB * K; i += kThreads) {
-        const int t = i / K, k = i - t * K;
-        const float v = (t < a.ntok) ? to_f32<XT>(x[(a.t0 + t) * a.ldx + k]) : 0.f;
-        xs[t * XSH + (k / S) * (S + 1) + (k % S)] = v;
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        const uint32_t v = warp_tot[lane];
+        uint32_t iv = v;
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t u = __shfl_up_sync(0xffffffffu, iv, o);
+            if (lane >= o) iv += u;
+        }
+        warp_tot[lane] = iv - v;                             // exclusive per warp
     }
     __syncthreads();
-
-    const int my_tiles =
-        (blockIdx.x < (unsigned)a.ntiles) ? (a.ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-    auto issue = [&](int j) {
-        const int tile = blockIdx.x + j * gridDim.x;
-        const int s = j % nst;
-        const int r0 = tile * RB;
-        const int rows = min(RB, a.M - r0);
-        const int64_t sb = a.rbs[r0];
-        const int64_t eb = (r0 + rows < a.M) ? a.rbs[r0 + rows] : a.total_bits;
-        const int64_t b0 = (sb >> 3) & ~(int64_t)15;
-        const int64_t b1 = (((eb + 7) >> 3) + 15 & ~(int64_t)15) + 32;
-        if (b1 - b0 <= (int64_t)a.stage_cap && b1 <= a.stream_bytes && b0 >= 0) {
-            b0s[s] = b0;
-            mbar_arrive_expect_tx(&bar[s], (uint32_t)(b1 - b0));
-            bulk_g2s(stg + (size_t)s * a.stage_cap, a.stream + b0, (uint32_t)(b1 - b0), &bar[s]);
-        } else {
-            b0s[s] = -1;  // tile too wide for a stage: decode it from global memory
-            mbar_arrive(&bar[s]);
-        }
-    };
-    if (tid == 0)
-        for (int j = 0; j < min(nst, my_tiles); ++j) issue(j);
-
-    const uint16_t *gsyms = blob_syms(a.tables);
-    const float *cb = CBS ? cb_s : a.codebook;
-    const uint32_t cmax = (uint32_t)(a.C - 1);
-    OT *out = static_cast<OT *>(a.out);
-    const int warp = tid >> 5, lane = tid & 31;
-    int j = 0;
-    for (; j < my_tiles; ++j) {
-        const int s = j % nst;
-        const bool ok = mbar_wait_bounded(&bar[s], (uint32_t)(j / nst) & 1u);
-        if (__syncthreads_or(!ok)) {
-            if (tid == 0) report(a.status, CBQ_FLAG_TIMEOUT, 0u);
-            break;
-        }
-        const int tile = blockIdx.x + j * gridDim.x;
-        const int r0 = tile * RB;
-        const int rows = min(RB, a.M - r0);
-        const int nc = rows * nch;
-        const int64_t b0 = b0s[s];
-        const uint32_t *sw = reinterpret_cast<const uint32_t *>(stg + (size_t)s * a.stage_cap);
-        for (int c = tid; c < nc; c += kThreads) {
-            const int rho = c / nch, q = c - rho * nch;
-            const int64_t r = r0 + rho;
-            const int64_t abs_bit = a.rbs[r] + (int64_t)a.chunk[r * nch + q];
-            const int nsym = min(S, K - q * S);
-            float acc[TB];
-#pragma unroll
-            for (int t = 0; t < TB; ++t) acc[t] = 0.f;
-            uint32_t bad = 0;
-            const float *xq = xs + q * (S + 1);
-            if (b0 >= 0)
-                huff_chunk_dot<TB, CBS>(sw, a.stage_cap / 4, (uint64_t)(abs_bit - b0 * 8), nsym, st,
-                                        gsyms, cb, cmax, xq, XSH, acc, bad);
-            else
-                huff_chunk_dot<TB, CBS>(reinterpret_cast<const uint32_t *>(a.stream),
-                                        (uint64_t)a.stream_bytes / 4, (uint64_t)abs_bit, nsym, st,
-                                        gsyms, cb, cmax, xq, XSH, acc, bad);
-            if (bad) report(a.status, CBQ_FLAG_CORRUPT, (uint32_t)r);
-#pragma unroll
-            for (int t = 0; t < TB; ++t) P[t * tile_chunks + c] = acc[t];
-        }
-        __syncthreads();
-        if (tid == 0 && j + nst < my_tiles) issue(j + nst);
-        for (int p = warp; p < rows * TB; p += kThreads / 32) {
-            const int rho = p / TB, t = p - rho * TB;
-            if (t >= a.ntok) continue;
-            const float *pp = P + t * tile_chunks + rho * nch;
-            float sum = 0.f;
-            for (int q = lane; q < nch; q += 32) sum += pp[q];
-            sum = warp_sum(sum);
-            if (lane == 0) {
-                const int r = r0 + rho;
-                if (a.bias) sum += a.bias[r];
-                out[(a.t0 + t) * a.ldo + r] = from_f32<OT>(sum);
+    uint32_t off = warp_tot[warp] + incl - mine;
+    uint32_t *sub = lut + kHfLutSize + 4;
+    uint32_t used_max = 0;
+    for (int j = 0; j < kPer; ++j) {
+        if (!depth[j]) continue;
+        const uint32_t p = (uint32_t)(p0 + j);
+        const uint32_t d = depth[j], n = 1u << d;
+        if (off + n <= (uint32_t)kHfSubMax) {
+            lut[p] = (off << 16) | (d << 8) | 0x80u;
+            for (uint32_t k = 0; k < n; ++k) {
+                const uint32_t w = (p << (32 - kHfLutBits)) | (k << (32 - kHfLutBits - d));
+                uint32_t sym;
+                const int L = code_len_at(tab, w, sym);
+                sub[off + k] = (L > kHfLutBits) ? ((payload(sym) << 16) | (uint32_t)L) : 0u;
             }
+            used_max = max(used_max, off + n);
         }
-        __syncthreads();
+        off += n;
     }
-    if (j < my_tiles && tid == 0) {
-        for (int jj = j; jj < min(j + nst, my_tiles); ++jj)
-            mbar_wait_bounded(&bar[jj % nst], (uint32_t)(jj / nst) & 1u);
-    }
+    used_max = __reduce_max_sync(0xffffffffu, used_max);
+    if (lane == 0) atomicMax(&lut[kHfLutSize + 1], used_max);
+    if (threadIdx.x == 0) lut[kHfLutSize] = exact ? 1u : 0u;
 }
 
 // ---------------------------------------------------------------- decode / embedding
@@ -435,50 +296,37 @@ __global__ void k_huff_encode(const uint16_t *idx, int64_t n, const uint32_t *co
 // ---------------------------------------------------------------- planning
 
 struct HuffPlan {
-    int RB = 0, nst = 0, TB = 0, ntiles = 0, grid = 0;
-    uint32_t stage_cap = 0;
+    int TB = 0, grid = 0;
+    uint32_t cap = 0;
     size_t smem = 0;
-    bool cbs = true;
 };
 
-size_t huff_smem(int C, bool cbs, int K, int RB, int TB, int nst, uint32_t cap) {
-    const int nch = (K + S - 1) / S;
-    size_t s = 256 + a128(sizeof(SmemTables));
-    if (cbs) s += a128((size_t)C * 4);
-    s += a128((size_t)TB * nch * (S + 1) * 4);
-    s += a128((size_t)TB * RB * nch * 4);
-    s += (size_t)nst * cap;
-    return s;
-}
-
-bool plan_huff(int64_t M, int64_t K, int64_t C, int64_t T, int64_t total_bits, HuffPlan &p) {
+bool plan_huff(int64_t M, int64_t K, int64_t T, int64_t total_bits, int xbytes, HuffPlan &p) {
     if (M <= 0 || K <= 0 || M >= (1ll << 31) || K > (1 << 18)) return false;
-    const int nch = (int)((K + S - 1) / S);
     const double avg = std::max(1.0, (double)total_bits / ((double)M * (double)K));
-    int RB = std::min(64, 256 / std::gcd(nch, 256));
-    auto cap_of = [&](int rb) {
-        return (uint32_t)cbq_host::align_up((int64_t)(rb * (double)K * avg / 8.0 * 1.3) + 128, 128);
-    };
-    while (RB > 1 && cap_of(RB) > 48 * 1024) RB /= 2;
-    const uint32_t cap = cap_of(RB);
-    const bool cbs = C <= kMaxCbSmem;
-    const size_t budget = (size_t)cbq_host::max_smem_optin() - 1024;
+    const int64_t seg = std::min<int64_t>(K, kHfSeg);
+    p.cap = (uint32_t)std::max<int64_t>(512, cbq_host::align_up((int64_t)(seg * avg / 8.0 * 1.15) + 96, 128));
+    const size_t budget = (size_t)cbq_host::max_smem_optin() - 256;
+    const size_t ring = (size_t)kHfWarps * kHfSlots * p.cap;
     int TB = 8;
     while (TB > 1 && TB > T) TB /= 2;
-    while (TB > 1 && huff_smem((int)C, cbs, (int)K, RB, TB, 2, cap) > budget) TB /= 2;
-    if (huff_smem((int)C, cbs, (int)K, RB, TB, 2, cap) > budget) return false;
-    int nst = 2;
-    while (nst < kMaxStages && huff_smem((int)C, cbs, (int)K, RB, TB, nst + 1, cap) <= budget) ++nst;
-    p.RB = RB; p.TB = TB; p.nst = nst; p.stage_cap = cap; p.cbs = cbs;
-    p.smem = huff_smem((int)C, cbs, (int)K, RB, TB, nst, cap);
-    p.ntiles = (int)((M + RB - 1) / RB);
-    p.grid = std::min(p.ntiles, cbq_host::sm_count());
+    while (TB > 1 && huff_prefix_bytes((int)K, TB, xbytes) + ring > budget) TB /= 2;
+    if (huff_prefix_bytes((int)K, TB, xbytes) + ring > budget) return false;
+    p.TB = TB;
+    p.smem = huff_prefix_bytes((int)K, TB, xbytes) + ring;
+    p.grid = cbq_host::sm_count();
     return true;
 }
 
-template <int TB, bool CBS, typename XT, typename OT>
+int64_t huff_workspace_bytes(int64_t M, int64_t K, int64_t T) {
+    const int64_t nseg = ((K + S - 1) / S + 31) / 32;
+    const int64_t TB = T >= 8 ? 8 : T >= 4 ? 4 : T >= 2 ? 2 : 1;
+    return cbq_host::align_up(M * nseg * TB * 4, 256) + cbq_host::align_up(M * 4, 256);
+}
+
+template <int TB, typename XT>
 int launch_huff_t(const HuffArgs &a, const HuffPlan &p, cudaStream_t s) {
-    auto kern = k_linear_huff<TB, CBS, XT, OT>;
+    auto kern = k_linear_huff<TB, XT>;
     static std::mutex mu;
     static size_t configured[64] = {0};
     int dev = 0;
@@ -491,29 +339,23 @@ int launch_huff_t(const HuffArgs &a, const HuffPlan &p, cudaStream_t s) {
             configured[dev & 63] = p.smem;
         }
     }
-    kern<<<p.grid, kThreads, p.smem, s>>>(a);
+    kern<<<p.grid, kHfWarps * 32, p.smem, s>>>(a);
     CBQ_CUDA_TRY(cudaGetLastError());
     return CBQ_OK;
 }
 
-template <bool CBS, typename XT, typename OT>
-int launch_huff_tb(const HuffArgs &a, const HuffPlan &p, cudaStream_t s) {
-    switch (p.TB) {
-        case 1: return launch_huff_t<1, CBS, XT, OT>(a, p, s);
-        case 2: return launch_huff_t<2, CBS, XT, OT>(a, p, s);
-        case 4: return launch_huff_t<4, CBS, XT, OT>(a, p, s);
-        case 8: return launch_huff_t<8, CBS, XT, OT>(a, p, s);
-    }
-    return CBQ_ERR_UNSUPPORTED;
-}
-
-template <typename XT, typename OT>
+template <typename XT>
 int linear_huff_impl(HuffArgs a, int64_t T, const HuffPlan &p, cudaStream_t s) {
     for (int64_t t0 = 0; t0 < T; t0 += p.TB) {
         a.t0 = t0;
         a.ntok = (int)std::min<int64_t>(p.TB, T - t0);
-        const int rc = p.cbs ? launch_huff_tb<true, XT, OT>(a, p, s)
-                             : launch_huff_tb<false, XT, OT>(a, p, s);
+        int rc = CBQ_ERR_UNSUPPORTED;
+        switch (p.TB) {
+            case 1: rc = launch_huff_t<1, XT>(a, p, s); break;
+            case 2: rc = launch_huff_t<2, XT>(a, p, s); break;
+            case 4: rc = launch_huff_t<4, XT>(a, p, s); break;
+            case 8: rc = launch_huff_t<8, XT>(a, p, s); break;
+        }
         if (rc != CBQ_OK) return rc;
     }
     return CBQ_OK;
@@ -603,38 +445,62 @@ extern "C" int cbq_huff_chunk_table(const uint8_t *stream_dev, int64_t stream_by
     return CBQ_OK;
 }
 
+extern "C" int64_t cbq_huff_decode_lut_bytes(void) { return (int64_t)kHfLutWords * 4; }
+
+extern "C" int cbq_huff_build_decode_lut(const void *tables_dev, const float *codebook_dev, int64_t C,
+                                         uint32_t *lut_dev, void *stream) {
+    if (!tables_dev || !codebook_dev || !lut_dev || C < 1 || C > 65536) return CBQ_ERR_ARG;
+    if (reinterpret_cast<uintptr_t>(lut_dev) & 15) return CBQ_ERR_ARG;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    CBQ_CUDA_TRY(cudaMemsetAsync(lut_dev, 0, (size_t)kHfLutWords * 4, s));
+    k_huff_build_lut<<<1, 1024, 0, s>>>(static_cast<const HuffTables *>(tables_dev), codebook_dev, (int)C,
+                                        lut_dev);
+    CBQ_CUDA_TRY(cudaGetLastError());
+    return CBQ_OK;
+}
+
+extern "C" int64_t cbq_linear_huff_workspace_bytes(int64_t M, int64_t K, int64_t T) {
+    if (M < 0 || K < 0 || T < 0) return -1;
+    return huff_workspace_bytes(M, K, T);
+}
+
 extern "C" int cbq_linear_huff(const void *x_dev, int x_dtype, int64_t T, int64_t ldx,
                                const uint8_t *stream_dev, int64_t stream_bytes,
-                               const void *tables_dev, const int64_t *rbs_dev,
-                               const uint32_t *chunk_dev, int64_t total_bits,
+                               const void *tables_dev, const uint32_t *lut_dev,
+                               const int64_t *rbs_dev, const uint32_t *chunk_dev, int64_t total_bits,
                                const float *codebook_dev, int64_t C, int64_t M, int64_t K,
                                const float *bias_dev, void *out_dev, int out_dtype, int64_t ldo,
-                               uint32_t *status_dev, void *stream) {
+                               void *workspace_dev, int64_t workspace_bytes, uint32_t *status_dev,
+                               void *stream) {
     if (T < 0 || M < 0 || K < 0 || C < 1 || C > 65536 || total_bits < 0) return CBQ_ERR_ARG;
     if ((x_dtype != CBQ_F32 && x_dtype != CBQ_BF16) || (out_dtype != CBQ_F32 && out_dtype != CBQ_BF16))
         return CBQ_ERR_ARG;
     if (T == 0 || M == 0) return CBQ_OK;
-    if (!out_dev || !codebook_dev || !x_dev || !stream_dev || !tables_ok(tables_dev) || !rbs_dev ||
-        !chunk_dev)
+    if (!out_dev || !codebook_dev || !x_dev || !stream_dev || !tables_ok(tables_dev) || !lut_dev ||
+        !rbs_dev || !chunk_dev)
         return CBQ_ERR_ARG;
     if (ldx < K || ldo < M) return CBQ_ERR_ARG;
     if (stream_bytes < cbq_huff_stream_bytes((total_bits + 7) / 8)) return CBQ_ERR_ARG;
-    if (reinterpret_cast<uintptr_t>(stream_dev) & 15) return CBQ_ERR_ARG;
+    if ((reinterpret_cast<uintptr_t>(stream_dev) & 15) || (reinterpret_cast<uintptr_t>(lut_dev) & 15))
+        return CBQ_ERR_ARG;
+    if (workspace_dev && workspace_bytes < huff_workspace_bytes(M, K, T)) return CBQ_ERR_ARG;
     HuffPlan p;
-    if (!plan_huff(M, K, C, T, total_bits, p)) return CBQ_ERR_UNSUPPORTED;
+    if (!plan_huff(M, K, T, total_bits, x_dtype == CBQ_BF16 ? 2 : 4, p)) return CBQ_ERR_UNSUPPORTED;
     HuffArgs a{};
     a.x = x_dev; a.ldx = ldx; a.stream = stream_dev; a.stream_bytes = stream_bytes;
-    a.tables = static_cast<const HuffTables *>(tables_dev); a.rbs = rbs_dev; a.chunk = chunk_dev;
-    a.total_bits = total_bits; a.codebook = codebook_dev; a.C = (int)C; a.M = (int)M; a.K = (int)K;
-    a.bias = bias_dev; a.out = out_dev; a.ldo = ldo; a.RB = p.RB; a.ntiles = p.ntiles;
-    a.nst = p.nst; a.stage_cap = p.stage_cap; a.status = status_dev;
+    a.tables = static_cast<const HuffTables *>(tables_dev); a.lut = lut_dev; a.rbs = rbs_dev;
+    a.chunk = chunk_dev; a.total_bits = total_bits; a.codebook = codebook_dev; a.C = (int)C;
+    a.M = (int)M; a.K = (int)K; a.nch = (int)((K + S - 1) / S); a.nseg = (a.nch + 31) / 32;
+    a.bias = bias_dev; a.out = out_dev; a.ldo = ldo; a.out_bf16 = out_dtype == CBQ_BF16;
+    a.cap = p.cap; a.status = status_dev;
+    if (workspace_dev) {
+        const int64_t pb = cbq_host::align_up(M * (int64_t)a.nseg * p.TB * 4, 256);
+        a.part = static_cast<float *>(workspace_dev);
+        a.cnt = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(workspace_dev) + pb);
+    }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (x_dtype == CBQ_F32 && out_dtype == CBQ_F32) return linear_huff_impl<float, float>(a, T, p, s);
-    if (x_dtype == CBQ_BF16 && out_dtype == CBQ_BF16)
-        return linear_huff_impl<__nv_bfloat16, __nv_bfloat16>(a, T, p, s);
-    if (x_dtype == CBQ_BF16 && out_dtype == CBQ_F32)
-        return linear_huff_impl<__nv_bfloat16, float>(a, T, p, s);
-    return linear_huff_impl<float, __nv_bfloat16>(a, T, p, s);
+    if (x_dtype == CBQ_BF16) return linear_huff_impl<__nv_bfloat16>(a, T, p, s);
+    return linear_huff_impl<float>(a, T, p, s);
 }
 
 extern "C" int cbq_embedding_huff(const int64_t *ids_dev, int64_t T, const uint8_t *stream_dev,

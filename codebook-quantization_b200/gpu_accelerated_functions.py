@@ -115,6 +115,17 @@ class GPUAcceleratedLinear:
         need = (self.M * self.K * self.bits + 7) // 8
         self.packed = padded_device_bytes(_stream_prefix(indices_np, need, name), self.nbytes,
                                           self.device)
+        self._ws = {}                      # token-block size -> zero-filled workspace
+
+    def workspace(self, T: int) -> torch.Tensor:
+        """Zero-filled workspace for T-token calls (the kernels leave it zeroed)."""
+        key = min(int(T), 8)
+        ws = self._ws.get(key)
+        if ws is None:
+            n = _lib.query("cbq_linear_fixed_workspace_bytes", self.M, self.K, key)
+            ws = torch.zeros(max(n, 16), dtype=torch.uint8, device=self.device)
+            self._ws[key] = ws
+        return ws
 
     def __call__(self, x: torch.Tensor, bias: torch.Tensor = None, out: torch.Tensor = None,
                  out_dtype: torch.dtype = None) -> torch.Tensor:
@@ -135,10 +146,12 @@ class GPUAcceleratedLinear:
         b = None
         if bias is not None:
             b = bias.to(device=self.device, dtype=torch.float32).contiguous()
+        ws = self.workspace(T)
         _lib.call("cbq_linear_fixed", x2.data_ptr(), xcode, T, x2.stride(0) if T > 1 else self.K,
                   self.packed.data_ptr(), self.nbytes, self.codebook.data_ptr(), self.C, self.bits,
                   self.M, self.K, None if b is None else b.data_ptr(), out.data_ptr(), ocode,
-                  out.stride(0) if T > 1 else self.M, device_stream(self.device))
+                  out.stride(0) if T > 1 else self.M, ws.data_ptr(), ws.numel(),
+                  device_stream(self.device))
         res = out.reshape(*lead, self.M)
         return res if res.dtype == want else res.to(want)
 

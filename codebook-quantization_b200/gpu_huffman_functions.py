@@ -144,6 +144,21 @@ class HuffmanCodebookLinear:
         self.hs = HuffmanStream(name, huff_stream, huff_lengths, huff_n, self.shape,
                                 huff_row_bit_starts, self.device)
         self.status = self.hs.status
+        nl = _lib.query("cbq_huff_decode_lut_bytes")
+        self.lut = torch.zeros(nl // 4, dtype=torch.int32, device=self.device)
+        _lib.call("cbq_huff_build_decode_lut", self.hs.tables.data_ptr(), self.codebook.data_ptr(), self.C,
+                  self.lut.data_ptr(), device_stream(self.device))
+        self._ws = {}
+
+    def workspace(self, T: int) -> torch.Tensor:
+        """Zero-filled workspace for T-token calls (the kernels leave it zeroed)."""
+        key = min(int(T), 8)
+        ws = self._ws.get(key)
+        if ws is None:
+            n = _lib.query("cbq_linear_huff_workspace_bytes", self.M, self.K, key)
+            ws = torch.zeros(max(n, 16), dtype=torch.uint8, device=self.device)
+            self._ws[key] = ws
+        return ws
 
     def __call__(self, x: torch.Tensor, bias: torch.Tensor = None, out: torch.Tensor = None,
                  out_dtype: torch.dtype = None) -> torch.Tensor:
@@ -161,11 +176,13 @@ class HuffmanCodebookLinear:
         ocode = _lib.CBQ_BF16 if out.dtype == torch.bfloat16 else _lib.CBQ_F32
         b = None if bias is None else bias.to(device=self.device, dtype=torch.float32).contiguous()
         hs = self.hs
+        ws = self.workspace(T)
         _lib.call("cbq_linear_huff", x2.data_ptr(), xcode, T, x2.stride(0) if T > 1 else self.K,
-                  hs.stream.data_ptr(), hs.nbytes, hs.tables.data_ptr(), hs.rbs.data_ptr(),
-                  hs.chunk.data_ptr(), hs.total_bits, self.codebook.data_ptr(), self.C, self.M, self.K,
-                  None if b is None else b.data_ptr(), out.data_ptr(), ocode,
-                  out.stride(0) if T > 1 else self.M, hs.status.data_ptr(), device_stream(self.device))
+                  hs.stream.data_ptr(), hs.nbytes, hs.tables.data_ptr(), self.lut.data_ptr(),
+                  hs.rbs.data_ptr(), hs.chunk.data_ptr(), hs.total_bits, self.codebook.data_ptr(), self.C,
+                  self.M, self.K, None if b is None else b.data_ptr(), out.data_ptr(), ocode,
+                  out.stride(0) if T > 1 else self.M, ws.data_ptr(), ws.numel(), hs.status.data_ptr(),
+                  device_stream(self.device))
         res = out.reshape(*lead, self.M)
         return res if res.dtype == want else res.to(want)
 

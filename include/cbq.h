@@ -80,6 +80,11 @@ int cbq_version(void);
  * reference pads +4 bytes on the GPU (src/gpu_accelerated_functions.py:860-864). */
 int64_t cbq_fixed_stream_bytes(int64_t M, int64_t K, int bits);
 
+/* Workspace bytes cbq_linear_fixed may use for an M x K matrix and T tokens
+ * (rows split between warps leave piece sums and an arrival counter there).
+ * The caller zero-fills it once; every call leaves it zeroed again. */
+int64_t cbq_linear_fixed_workspace_bytes(int64_t M, int64_t K, int64_t T);
+
 /* out[t, r] = sum_k x[t, k] * codebook[min(idx(r*K + k), C-1)] (+ bias[r]).
  * Replaces fused_compressed_linear (src/gpu_accelerated_functions.py:238-274)
  * and ck_linear_f32 (rocm/compressed_kernel.hip:607-616).
@@ -87,12 +92,18 @@ int64_t cbq_fixed_stream_bytes(int64_t M, int64_t K, int bits);
  *   packed_dev fixed-width stream, packed_bytes >= cbq_fixed_stream_bytes()
  *   codebook_dev fp32[C], C >= 1;  bits in [1, 16]
  *   bias_dev   fp32[M] or NULL
- *   out_dev    [T, ldo] rows of M outputs, dtype out_dtype (overwritten) */
+ *   out_dev    [T, ldo] rows of M outputs, dtype out_dtype (overwritten)
+ *   workspace_dev  NULL, or a zero-filled buffer of at least
+ *              cbq_linear_fixed_workspace_bytes(M, K, T) bytes: lets the
+ *              kernel balance work at 1024-index granularity instead of
+ *              whole rows.  Calls sharing one workspace must not overlap on
+ *              the GPU (the same stream is fine). */
 int cbq_linear_fixed(const void *x_dev, int x_dtype, int64_t T, int64_t ldx,
                      const uint8_t *packed_dev, int64_t packed_bytes,
                      const float *codebook_dev, int64_t C, int bits,
                      int64_t M, int64_t K, const float *bias_dev,
-                     void *out_dev, int out_dtype, int64_t ldo, void *stream);
+                     void *out_dev, int out_dtype, int64_t ldo,
+                     void *workspace_dev, int64_t workspace_bytes, void *stream);
 
 /* out[t, h] = codebook[min(idx(ids[t]*H + h), C-1)] for a [vocab, H] table.
  * Replaces fused_compressed_embedding (src/gpu_accelerated_functions.py:276-307).
@@ -144,17 +155,34 @@ int cbq_huff_chunk_table(const uint8_t *stream_dev, int64_t stream_bytes,
                          int64_t M, int64_t K, int64_t total_bits,
                          uint32_t *chunk_dev, uint32_t *status_dev, void *stream);
 
+/* Load-time pass: the two-level decode table the fused GEMV reads.  For each
+ * 14-bit prefix: the length of the code it starts with and either the
+ * codebook value (bf16 bits, when every codebook value is exactly a bf16: all
+ * lossless codebooks) or the symbol; prefixes of longer codes point into a
+ * second-level table.  lut_dev holds cbq_huff_decode_lut_bytes() bytes,
+ * 16-byte aligned. */
+int64_t cbq_huff_decode_lut_bytes(void);
+int cbq_huff_build_decode_lut(const void *tables_dev, const float *codebook_dev, int64_t C,
+                              uint32_t *lut_dev, void *stream);
+
+/* Workspace bytes cbq_linear_huff may use (same contract as
+ * cbq_linear_fixed_workspace_bytes). */
+int64_t cbq_linear_huff_workspace_bytes(int64_t M, int64_t K, int64_t T);
+
 /* Fused Huffman decode + GEMV: same result as cbq_linear_fixed on the
  * decoded indices.  Replaces huffman_decode_to_i32 + huffman_i32_linear
  * (src/gpu_huffman_functions.py:297-370), without the int32 [M,K] buffer.
- * total_bits = 8 * (stream_len - 4): the end of the last row. */
+ * total_bits = 8 * (stream_len - 4): the end of the last row.  workspace_dev
+ * may be NULL (work is then balanced in whole rows). */
 int cbq_linear_huff(const void *x_dev, int x_dtype, int64_t T, int64_t ldx,
                     const uint8_t *stream_dev, int64_t stream_bytes,
-                    const void *tables_dev, const int64_t *row_bit_starts_dev,
+                    const void *tables_dev, const uint32_t *lut_dev,
+                    const int64_t *row_bit_starts_dev,
                     const uint32_t *chunk_dev, int64_t total_bits,
                     const float *codebook_dev, int64_t C,
                     int64_t M, int64_t K, const float *bias_dev,
                     void *out_dev, int out_dtype, int64_t ldo,
+                    void *workspace_dev, int64_t workspace_bytes,
                     uint32_t *status_dev, void *stream);
 
 /* Huffman embedding: decodes only the requested rows (the reference decodes

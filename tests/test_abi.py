@@ -47,7 +47,7 @@ def test_size_queries():
 def test_argument_errors_are_detected_on_host():
     lib = L.lib()
     args = dict(x=None, xd=0, T=1, ldx=8, p=None, pb=1 << 20, cb=None, C=4, bits=4, M=8, K=8,
-                bias=None, out=None, od=0, ldo=8, s=None)
+                bias=None, out=None, od=0, ldo=8, ws=None, wsb=0, s=None)
     base = list(args.values())
 
     def call(**kw):
@@ -62,8 +62,9 @@ def test_argument_errors_are_detected_on_host():
     assert call(T=0) == L.CBQ_OK                   # nothing to do
     assert call(x=1, p=16, cb=4, out=8, ldx=4) == L.CBQ_ERR_ARG       # ldx < K
     assert call(x=1, p=16, cb=4, out=8, pb=10) == L.CBQ_ERR_ARG       # stream too short
+    assert call(x=1, p=16, cb=4, out=8, ws=64, wsb=1) == L.CBQ_ERR_ARG  # workspace too small
     assert lib.cbq_pack_fixed(None, 10, 0, None, 64, None) == L.CBQ_ERR_ARG
-    assert len(base) == 16
+    assert len(base) == 18
 
 
 def _blob_view(blob):
