@@ -105,6 +105,29 @@ int cbq_linear_fixed(const void *x_dev, int x_dtype, int64_t T, int64_t ldx,
                      void *out_dev, int out_dtype, int64_t ldo,
                      void *workspace_dev, int64_t workspace_bytes, void *stream);
 
+/* Size of the device array built into the library that
+ * cbq_linear_fixed_noalloc uses as its workspace (8 MiB on every GPU that
+ * loads the library, until the process exits). */
+#define CBQ_NOALLOC_SCRATCH_BYTES (8u << 20)
+
+/* cbq_linear_fixed for callers that cannot allocate device memory (for
+ * example a plugin inside a host framework that owns all device memory and
+ * hands it only inputs and outputs).  No counterpart in the reference.
+ * Same arguments and result as cbq_linear_fixed, but the workspace comes from
+ * the built-in array above; no cudaMalloc/cudaFree is ever called.
+ *   - Returns CBQ_ERR_ARG when the matrix needs more workspace than
+ *     CBQ_NOALLOC_SCRATCH_BYTES (cbq_linear_fixed_workspace_bytes(M, K, T)).
+ *   - The first call on a device looks the array's device address up; make
+ *     that first call before any stream capture on that device.
+ *   - All calls share the one array: calls that overlap on the GPU (different
+ *     streams, or several host threads) race and give wrong results.  Each
+ *     call clears the part it uses on its stream before launching. */
+int cbq_linear_fixed_noalloc(const void *x_dev, int x_dtype, int64_t T, int64_t ldx,
+                             const uint8_t *packed_dev, int64_t packed_bytes,
+                             const float *codebook_dev, int64_t C, int bits,
+                             int64_t M, int64_t K, const float *bias_dev,
+                             void *out_dev, int out_dtype, int64_t ldo, void *stream);
+
 /* out[t, h] = codebook[min(idx(ids[t]*H + h), C-1)] for a [vocab, H] table.
  * Replaces fused_compressed_embedding (src/gpu_accelerated_functions.py:276-307).
  * Token ids outside [0, vocab) are an argument error detected on the device:
