@@ -37,6 +37,11 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
                  ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 
+// Plain arrive (release semantics at CTA scope) by the calling thread.
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -47,15 +52,34 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait that may suspend the thread for up to `hint_ns` while the phase is
+// incomplete (the hardware wakes it when the phase completes), so a waiting
+// warp does not spin through the issue slots.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns) : "memory");
+    return ok != 0;
+}
+
 // Wait for phase `parity` of `bar` to complete, giving up after kWaitNs.
 // Returns false on timeout (the caller records CBQ_FLAG_TIMEOUT and stops).
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
         if (global_timer_ns() - t0 > kWaitNs) return false;
     }
+}
+
+// Order this thread's earlier shared-memory accesses (generic proxy) before
+// its later bulk copies into the same bytes (async proxy).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // 1-D bulk copy global -> this CTA's shared memory, completing on `bar`.

@@ -13,10 +13,13 @@
 #include <mutex>
 
 #include "cbq_fixed_kernel.cuh"
+#include "cbq_gemv_kernel.cuh"
 
 namespace cbq {
 template <int BITS>
 int launch_fixed_bits(int TB, bool x_bf16, const FixedArgs &a, size_t smem, int grid, cudaStream_t s);
+template <int BITS>
+int launch_gemv_bits(int TB, bool x_bf16, const GemvArgs &a, size_t smem, int grid, cudaStream_t s);
 }
 
 namespace {
@@ -130,6 +133,45 @@ int64_t workspace_bytes_for(int64_t M, int64_t K, int64_t T) {
     return cbq_host::align_up(M * nseg * TB * 4, 256) + cbq_host::align_up(M * 4, 256);
 }
 
+// Plan of the one/two-token kernel (k_gemv_fixed); false -> k_linear_fixed.
+struct GemvPlan {
+    int grid = 0, rows_per_cta = 0, nseg = 0;
+    uint32_t H = 0, NP = 0;
+    size_t smem = 0;
+};
+
+bool plan_gemv(int64_t M, int64_t K, int bits, int64_t C, int64_t T, GemvPlan &p) {
+    if (T < 1 || T > 2 || K <= 0 || K % 128 != 0 || K > (1 << 20) || M <= 0 || M >= (1ll << 31))
+        return false;
+    const int64_t sms = cbq_host::sm_count();
+    const int64_t rows = (M + sms - 1) / sms;
+    const int nseg = (int)((K + kGvSeg - 1) / kGvSeg);
+    const int64_t NP = (bits <= 14) ? std::max<int64_t>(C, 1ll << bits) : C;
+    const size_t budget = (size_t)cbq_host::max_smem_optin();
+    const size_t fixed = kGvBarBytes + gemv_part_bytes((int)rows, nseg, (int)T) + gemv_ring_bytes(bits);
+    if (fixed + a128((size_t)NP * 4) > budget) return false;
+    int64_t H = (int64_t)((budget - fixed - 128 - (size_t)NP * 4) / 124);
+    H = std::min<int64_t>(H, C);
+    p.grid = (int)((M + rows - 1) / rows);
+    p.rows_per_cta = (int)rows;
+    p.nseg = nseg;
+    p.H = (uint32_t)H;
+    p.NP = (uint32_t)NP;
+    p.smem = fixed + gemv_cb_bytes(p.H, p.NP);
+    return p.smem <= budget;
+}
+
+int launch_gemv(int bits, int TB, bool xbf16, const GemvArgs &a, size_t smem, int grid,
+                cudaStream_t s) {
+    switch (bits) {
+#define CBQ_B(n) case n: return launch_gemv_bits<n>(TB, xbf16, a, smem, grid, s);
+        CBQ_B(1) CBQ_B(2) CBQ_B(3) CBQ_B(4) CBQ_B(5) CBQ_B(6) CBQ_B(7) CBQ_B(8)
+        CBQ_B(9) CBQ_B(10) CBQ_B(11) CBQ_B(12) CBQ_B(13) CBQ_B(14) CBQ_B(15) CBQ_B(16)
+#undef CBQ_B
+    }
+    return CBQ_ERR_ARG;
+}
+
 int launch_bits(int bits, int TB, bool xbf16, const FixedArgs &a, size_t smem, int grid,
                 cudaStream_t s) {
     switch (bits) {
@@ -148,6 +190,16 @@ int linear_fixed_impl(const void *x, int x_dtype, int64_t T, int64_t ldx, const 
     FixedPlan p;
     const bool aligned = (reinterpret_cast<uintptr_t>(packed) & 15) == 0;
     const int xbytes = x_dtype == CBQ_BF16 ? 2 : 4;
+    const bool x_aligned = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (ldx * xbytes) % 16 == 0;
+    GemvPlan g;
+    if (aligned && x_aligned && plan_gemv(M, K, bits, C, T, g)) {
+        GemvArgs a{};
+        a.x = x; a.ldx = ldx; a.t0 = 0; a.ntok = (int)T; a.packed = packed; a.codebook = cb;
+        a.C = (int)C; a.M = (int)M; a.K = (int)K; a.nseg = g.nseg; a.rows_per_cta = g.rows_per_cta;
+        a.bias = bias; a.out = out; a.ldo = ldo; a.out_bf16 = out_dtype == CBQ_BF16;
+        a.H = g.H; a.NP = g.NP; a.m128 = 128u; a.m4 = 4u; a.status = nullptr;
+        return launch_gemv(bits, (int)T, x_dtype == CBQ_BF16, a, g.smem, g.grid, s);
+    }
     if (aligned && plan_fixed(M, K, bits, C, T, xbytes, p)) {
         FixedArgs a{};
         a.x = x; a.ldx = ldx; a.packed = packed; a.codebook = cb; a.C = (int)C;

@@ -39,6 +39,7 @@ namespace cbq {
 constexpr int kFxWarps = 16;      // warps per CTA
 constexpr int kFxSeg = 1024;      // indices per unit
 constexpr int kFxSlots = 3;       // ring slots per warp
+static_assert(kFxWarps * kFxSlots * 8 <= 512, "the mbarriers occupy the first 512 bytes of shared memory");
 
 struct FixedArgs {
     const void *x;

@@ -1,0 +1,354 @@
+// cbq_gemv_kernel.cuh -- fixed-width decode GEMV for one or two tokens
+// (sm_100a).
+//
+// out[t, r] = sum_k x[t, k] * cb[min(idx(r*K + k), C-1)], idx LSB-first b-bit
+// fields (reference src/bitpack.py:32-94, src/compressed_matmul.c:334-347).
+//
+// The hot loop is bound by the integer pipe and by shared-memory wavefronts,
+// so this kernel spends as few of both as it can per index:
+//
+//   * Activations live in registers.  Every CTA owns a block of whole rows;
+//     inside it the (row, 1024-index segment) units are numbered
+//     segment-major and dealt to the warps in contiguous ranges, so a warp
+//     keeps the 32 activations of its lane's share of one segment in
+//     registers for many rows in a row.  Each unit's per-row sum goes to
+//     shared memory; after a CTA barrier the segment sums of every row are
+//     added in segment order (bitwise reproducible, no workspace, no atomics).
+//   * The codebook address costs two multiply-adds (FMA pipe) and one min
+//     (integer pipe).  The first H entries are replicated once per lane
+//     (entry c of lane j at c*128 + 4j: always bank j) and the other entries
+//     follow as a single copy (entry c >= H at H*128 + (c-H)*4), so
+//         addr(c) = min(c*128 + 4j, c*4 + H*124)
+//     picks the replicated copy exactly when c < H.  For b <= 14 the single
+//     copy is padded to 2^b entries with cb[C-1], which is the reference's
+//     clamp idx >= C -> C-1 without an instruction.  The multipliers arrive as
+//     kernel arguments so the compiler keeps them as multiply-adds.
+//   * Each warp streams its units through a private ring of shared-memory
+//     slots (one cp.async.bulk per unit, completing on the slot's mbarrier)
+//     and decodes two rows of a segment at once where it can; the first
+//     copies are issued before the codebook is built so that the DRAM latency
+//     overlaps the table fill.
+#pragma once
+#include "cbq_common.cuh"
+
+namespace cbq {
+
+#ifndef CBQ_GV_WARPS
+#define CBQ_GV_WARPS 16
+#endif
+#ifndef CBQ_GV_SLOTS
+#define CBQ_GV_SLOTS 3
+#endif
+#ifndef CBQ_GV_PAIR
+#define CBQ_GV_PAIR 1
+#endif
+constexpr int kGvWarps = CBQ_GV_WARPS;   // warps per CTA
+constexpr int kGvSeg = 1024;             // indices per unit (32 lanes x 32)
+constexpr int kGvSlots = CBQ_GV_SLOTS;   // ring slots per warp
+constexpr size_t kGvBarBytes = a128((size_t)kGvWarps * kGvSlots * 8);   // one mbarrier per slot
+static_assert(kGvWarps * 32 <= 1024 && kGvSlots >= 2, "gemv launch shape");
+
+struct GemvArgs {
+    const void *x;
+    int64_t ldx;
+    int64_t t0;          // first token of this launch
+    int ntok;            // tokens in this launch (<= TB)
+    const uint8_t *packed;
+    const float *codebook;
+    int C;
+    int M, K, nseg;
+    int rows_per_cta;
+    const float *bias;
+    void *out;
+    int64_t ldo;
+    int out_bf16;
+    uint32_t H;          // replicated codebook entries
+    uint32_t NP;         // entries held in shared memory (head + single copy)
+    uint32_t m128, m4;   // 128 and 4
+    uint32_t *status;
+};
+
+// Shared-memory layout: [barriers][row-segment sums][codebook][rings].
+__host__ __device__ inline size_t gemv_part_bytes(int rows_per_cta, int nseg, int TB) {
+    return a128((size_t)rows_per_cta * nseg * TB * 4);
+}
+__host__ __device__ inline size_t gemv_cb_bytes(uint32_t H, uint32_t NP) {
+    return a128((size_t)H * 128 + (size_t)(NP - H) * 4);
+}
+__host__ __device__ inline size_t gemv_ring_bytes(int bits) {
+    return (size_t)kGvWarps * kGvSlots * kGvSeg * bits / 8;
+}
+
+template <int BITS>
+__device__ __forceinline__ void gv_load_share(const uint32_t *p, uint32_t (&w)[BITS + 1]) {
+    // lane stride BITS words: 32-bit loads for odd BITS (conflict-free), wider
+    // loads for even BITS so the lanes' loads stay on distinct banks
+    if constexpr (BITS % 4 == 0) {
+#pragma unroll
+        for (int s = 0; s < BITS / 4; ++s) {
+            const uint4 v = reinterpret_cast<const uint4 *>(p)[s];
+            w[4 * s] = v.x; w[4 * s + 1] = v.y; w[4 * s + 2] = v.z; w[4 * s + 3] = v.w;
+        }
+    } else if constexpr (BITS % 2 == 0) {
+#pragma unroll
+        for (int s = 0; s < BITS / 2; ++s) {
+            const uint2 v = reinterpret_cast<const uint2 *>(p)[s];
+            w[2 * s] = v.x; w[2 * s + 1] = v.y;
+        }
+    } else {
+#pragma unroll
+        for (int s = 0; s < BITS; ++s) w[s] = p[s];
+    }
+    w[BITS] = 0u;
+}
+
+template <int BITS>
+__device__ __forceinline__ uint32_t gv_field(const uint32_t (&w)[BITS + 1], int i) {
+    const int bit = i * BITS, wi = bit >> 5, sh = bit & 31;
+    constexpr uint32_t mask = (1u << BITS) - 1u;
+    const uint32_t v = (sh + BITS <= 32) ? (w[wi] >> sh) : __funnelshift_r(w[wi], w[wi + 1], sh);
+    return v & mask;
+}
+
+__device__ __forceinline__ float gv_lds(uint32_t addr) {
+    float v;
+    asm("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+    return v;
+}
+
+// The 32 activations of lane `lane` in segment s, token row xr (zero past K).
+__device__ __forceinline__ void gv_load_x(const float *xr, int k0, int K, float (&v)[32]) {
+    if (k0 < K) {
+        const float4 *p = reinterpret_cast<const float4 *>(xr + k0);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const float4 f = __ldg(p + q);
+            v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+    }
+}
+__device__ __forceinline__ void gv_load_x(const __nv_bfloat16 *xr, int k0, int K, float (&v)[32]) {
+    if (k0 < K) {
+        const uint4 *p = reinterpret_cast<const uint4 *>(xr + k0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint4 f = __ldg(p + q);
+            const uint32_t u[4] = {f.x, f.y, f.z, f.w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+                v[8 * q + 2 * h] = __uint_as_float(u[h] << 16);
+                v[8 * q + 2 * h + 1] = __uint_as_float(u[h] & 0xffff0000u);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+    }
+}
+
+template <int BITS, int TB, typename XT>
+__global__ void __launch_bounds__(kGvWarps * 32, 1) k_gemv_fixed(const GemvArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr uint32_t kSegBytes = (uint32_t)kGvSeg * BITS / 8;
+    constexpr bool kPadded = BITS <= 14;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nseg = a.nseg, K = a.K;
+    const int64_t m0 = (int64_t)blockIdx.x * a.rows_per_cta;
+    if (m0 >= a.M) return;                                   // the whole CTA: no barrier pending
+    const int nrows = (int)min((int64_t)a.rows_per_cta, (int64_t)a.M - m0);
+
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem) + warp * kGvSlots;
+    float *part = reinterpret_cast<float *>(smem + kGvBarBytes);
+    uint8_t *cbs = smem + kGvBarBytes + gemv_part_bytes(a.rows_per_cta, nseg, TB);
+    uint8_t *ring = cbs + gemv_cb_bytes(a.H, a.NP) + (size_t)warp * kGvSlots * kSegBytes;
+
+    // this warp's units: u = s * nrows + rl (segment-major)
+    const int U = nrows * nseg;
+    const int u0 = (int)((int64_t)warp * U / kGvWarps);
+    const int u1 = (int)((int64_t)(warp + 1) * U / kGvWarps);
+    const int n = u1 - u0;
+
+    int is = u0 / nrows, irl = u0 - (u0 / nrows) * nrows, islot = 0;   // next unit to copy
+    auto issue_next = [&]() {                                // lane 0 only
+        const int cnt = min(kGvSeg, K - is * kGvSeg);
+        const uint32_t bytes = (uint32_t)cnt * BITS / 8;
+        mbar_arrive_expect_tx(&bars[islot], bytes);
+        bulk_g2s(ring + (size_t)islot * kSegBytes,
+                 a.packed + ((m0 + irl) * (int64_t)K + (int64_t)is * kGvSeg) * BITS / 8, bytes,
+                 &bars[islot]);
+        if (++irl == nrows) { irl = 0; ++is; }
+        if (++islot == kGvSlots) islot = 0;
+    };
+    if (lane == 0) {
+        for (int s = 0; s < kGvSlots; ++s) mbar_init(&bars[s], 1);
+        mbar_fence_init();
+        for (int i = 0; i < n && i < kGvSlots; ++i) issue_next();
+    }
+
+    // codebook: replicated head, then the single copy (padded for b <= 14).
+    // One load per entry; a head row (32 copies, 128 B) is written as eight
+    // 16-byte stores whose order is rotated by lane so that the eight lanes
+    // of each store phase hit distinct banks.
+    // All loads of a pass are issued before any store, so the pass costs one
+    // global-memory latency.
+    {
+        const uint32_t H = a.H, NP = a.NP;
+        const int cmax = a.C - 1;
+        constexpr int kT = kGvWarps * 32;
+        constexpr int kBatch = 8;
+        for (uint32_t e0 = 0; e0 < H; e0 += kT * kBatch) {
+            float v[kBatch];
+#pragma unroll
+            for (int j = 0; j < kBatch; ++j) {
+                const uint32_t e = e0 + j * kT + tid;
+                v[j] = e < H ? __ldg(a.codebook + min((int)e, cmax)) : 0.f;
+            }
+#pragma unroll
+            for (int j = 0; j < kBatch; ++j) {
+                const uint32_t e = e0 + j * kT + tid;
+                if (e < H) {
+                    const float4 v4 = make_float4(v[j], v[j], v[j], v[j]);
+                    float4 *row = reinterpret_cast<float4 *>(cbs + (size_t)e * 128);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) row[(q + lane) & 7] = v4;
+                }
+            }
+        }
+        float *tw = reinterpret_cast<float *>(cbs + (size_t)H * 128);
+        constexpr int kTB = 24;
+        for (uint32_t c0 = H; c0 < NP; c0 += kT * kTB) {
+            float v[kTB];
+#pragma unroll
+            for (int j = 0; j < kTB; ++j) {
+                const uint32_t c = c0 + j * kT + tid;
+                v[j] = c < NP ? __ldg(a.codebook + min((int)c, cmax)) : 0.f;
+            }
+#pragma unroll
+            for (int j = 0; j < kTB; ++j) {
+                const uint32_t c = c0 + j * kT + tid;
+                if (c < NP) tw[c - H] = v[j];
+            }
+        }
+    }
+    __syncthreads();
+
+    const uint32_t cb_base = smem_u32(cbs);
+    const uint32_t head_off = cb_base + (uint32_t)lane * 4u;
+    const uint32_t tail_off = cb_base + a.H * 124u;
+    const uint32_t m128 = a.m128, m4 = a.m4;
+    const uint32_t cmax = (uint32_t)(a.C - 1);
+    const XT *x = static_cast<const XT *>(a.x);
+
+    float xr[TB][32];
+    int xs = -1;                                             // segment whose x is loaded
+    int s = u0 / nrows, rl = u0 - (u0 / nrows) * nrows;      // unit being decoded
+    int slot = 0;
+    uint32_t phase = 0;
+    auto slot_words = [&](int sl) {
+        return reinterpret_cast<const uint32_t *>(ring + (size_t)sl * kSegBytes) + lane * BITS;
+    };
+    auto gather = [&](uint32_t c) {
+        if (!kPadded) c = min(c, cmax);
+        return gv_lds(min(c * m128 + head_off, c * m4 + tail_off));
+    };
+    int i = 0;
+    while (i < n) {
+        if (s != xs) {
+            const int k0 = s * kGvSeg + lane * 32;
+#pragma unroll
+            for (int t = 0; t < TB; ++t) {
+                if (t < a.ntok) gv_load_x(x + (a.t0 + t) * a.ldx, k0, K, xr[t]);
+                else {
+#pragma unroll
+                    for (int q = 0; q < 32; ++q) xr[t][q] = 0.f;
+                }
+            }
+            xs = s;
+        }
+        // Two rows of the same segment at once when the range allows: twice
+        // the independent gathers in flight per warp.
+        const bool two = CBQ_GV_PAIR && i + 1 < n && rl + 1 < nrows;
+        const int slot2 = slot + 1 == kGvSlots ? 0 : slot + 1;
+        const uint32_t phase2 = slot + 1 == kGvSlots ? phase ^ 1u : phase;
+        bool ok = mbar_wait_bounded(&bars[slot], phase);
+        if (two) ok = mbar_wait_bounded(&bars[slot2], phase2) && ok;
+        if (__any_sync(0xffffffffu, !ok)) {
+            if (lane == 0) report(a.status, CBQ_FLAG_TIMEOUT, (uint32_t)(m0 + rl));
+            break;
+        }
+        float acc[2][2][TB];
+#pragma unroll
+        for (int t = 0; t < TB; ++t) { acc[0][0][t] = acc[0][1][t] = acc[1][0][t] = acc[1][1][t] = 0.f; }
+        const bool live = s * kGvSeg + lane * 32 < K;
+        uint32_t w[BITS + 1], w2[BITS + 1];
+        if (live) {
+            gv_load_share<BITS>(slot_words(slot), w);
+            if (two) gv_load_share<BITS>(slot_words(slot2), w2);
+        }
+        if (live) {
+            if (two) {
+#pragma unroll
+                for (int q = 0; q < 32; ++q) {
+                    const float v = gather(gv_field<BITS>(w, q));
+                    const float v2 = gather(gv_field<BITS>(w2, q));
+#pragma unroll
+                    for (int t = 0; t < TB; ++t) {
+                        acc[0][q & 1][t] = fmaf(xr[t][q], v, acc[0][q & 1][t]);
+                        acc[1][q & 1][t] = fmaf(xr[t][q], v2, acc[1][q & 1][t]);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int q = 0; q < 32; ++q) {
+                    const float v = gather(gv_field<BITS>(w, q));
+#pragma unroll
+                    for (int t = 0; t < TB; ++t) acc[0][q & 1][t] = fmaf(xr[t][q], v, acc[0][q & 1][t]);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) {
+            if (i + kGvSlots < n) issue_next();
+            if (two && i + 1 + kGvSlots < n) issue_next();
+        }
+#pragma unroll
+        for (int t = 0; t < TB; ++t) {
+            const float tot = warp_sum(acc[0][0][t] + acc[0][1][t]);
+            if (lane == 0) part[((size_t)rl * nseg + s) * TB + t] = tot;
+            if (two) {
+                const float tot2 = warp_sum(acc[1][0][t] + acc[1][1][t]);
+                if (lane == 0) part[((size_t)(rl + 1) * nseg + s) * TB + t] = tot2;
+            }
+        }
+        const int step = two ? 2 : 1;
+        i += step;
+        rl += step;
+        if (rl == nrows) { rl = 0; ++s; }
+        slot += step;
+        if (slot >= kGvSlots) { slot -= kGvSlots; phase ^= 1u; }
+    }
+    if (i < n && lane == 0) {   // timed out: wait (bounded) for this warp's copies still in flight
+        for (int j = i; j < n && j < i + kGvSlots; ++j) {
+            mbar_wait_bounded(&bars[slot], phase);
+            if (++slot == kGvSlots) { slot = 0; phase ^= 1u; }
+        }
+    }
+    __syncthreads();
+
+    // rows: segment sums in segment order, + bias, in the output dtype
+    for (int r = tid; r < nrows; r += kGvWarps * 32) {
+        const float b = a.bias ? a.bias[m0 + r] : 0.f;
+        for (int t = 0; t < a.ntok; ++t) {
+            float sum = 0.f;
+            for (int q = 0; q < nseg; ++q) sum += part[((size_t)r * nseg + q) * TB + t];
+            const int64_t o = (a.t0 + t) * a.ldo + m0 + r;
+            if (a.out_bf16) static_cast<__nv_bfloat16 *>(a.out)[o] = __float2bfloat16_rn(sum + b);
+            else static_cast<float *>(a.out)[o] = sum + b;
+        }
+    }
+}
+
+}  // namespace cbq

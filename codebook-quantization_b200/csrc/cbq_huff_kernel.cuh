@@ -30,6 +30,8 @@ constexpr int kHfWarps = 16;
 constexpr int kHfChunk = CBQ_HUFF_CHUNK;         // symbols per chunk (64)
 constexpr int kHfSeg = 32 * kHfChunk;            // symbols per unit (2048)
 constexpr int kHfSlots = 2;
+static_assert((kHfWarps * kHfSlots + 1) * 8 <= 512 && kHfWarps * kHfSlots * 8 <= 512,
+              "barriers and slot bases each occupy a 512-byte region of shared memory");
 constexpr int kHfLutBits = 14;
 constexpr int kHfLutSize = 1 << kHfLutBits;
 constexpr int kHfSubMax = 6144;                  // second-level entries kept in shared memory
