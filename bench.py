@@ -390,7 +390,7 @@ def main():
                          "timing": "CUDA-graph replay of the 36 gate_proj launches, CUDA events"},
             "e2e": {"value": args.batch * 1000.0 / ms_e2e, "unit": "tok/s",
                     "h2d_bytes_per_step": 8 * args.batch, "d2h_bytes_per_step": 8 * args.batch},
-            "gpu_launches": args.steps * n_lin,
+            "gpu_launches": args.steps * dec.launches_per_step(),
             "clocks": clk.summary(),
         }
         if cpu:

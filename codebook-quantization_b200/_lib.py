@@ -32,6 +32,8 @@ SIGNATURES = {
     "cbq_linear_fixed_workspace_bytes": (_I64, [_I64, _I64, _I64]),
     "cbq_linear_fixed": (_INT, [_P, _INT, _I64, _I64, _P, _I64, _P, _I64, _INT, _I64, _I64, _P, _P,
                                 _INT, _I64, _P, _I64, _P]),
+    "cbq_linear_fixed_multi": (_INT, [_P, _INT, _I64, _I64, _INT, _P, _P, _P, _P, _I64, _INT, _I64, _P,
+                                      _P, _P, _P, _INT, _INT, _P]),
     "cbq_linear_fixed_noalloc": (_INT, [_P, _INT, _I64, _I64, _P, _I64, _P, _I64, _INT, _I64, _I64, _P,
                                         _P, _INT, _I64, _P]),
     "cbq_embedding_fixed": (_INT, [_P, _I64, _P, _I64, _P, _I64, _INT, _I64, _I64, _P, _INT, _P, _P]),
@@ -51,7 +53,12 @@ SIGNATURES = {
                                   _P]),
     "cbq_huff_decode_indices": (_INT, [_P, _I64, _P, _P, _P, _I64, _I64, _P, _P, _P]),
     "cbq_huff_encode": (_INT, [_P, _I64, _P, _P, _P, _P, _I64, _P]),
+    "cbq_rmsnorm": (_INT, [_P, _P, _INT, _I64, _I64, _P, ct.c_float, _P, _P]),
+    "cbq_qk_norm_rope": (_INT, [_P, _P, _P, _INT, _I64, _I64, _I64, _I64, ct.c_float, _P, _P, _P, _P, _P,
+                                _P, _P, _P, _I64, _P]),
+    "cbq_attn_decode": (_INT, [_P, _P, _P, _INT, _I64, _I64, _I64, _I64, _I64, _P, ct.c_float, _P, _P]),
 }
+CBQ_EPI_STORE, CBQ_EPI_RESIDUAL, CBQ_EPI_SILU_MUL = 0, 1, 2
 
 
 class CbqError(RuntimeError):

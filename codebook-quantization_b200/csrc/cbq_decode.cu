@@ -1,0 +1,270 @@
+// cbq_decode.cu -- the per-token transformer-block kernels around the
+// compressed linear layers of a decode step (sm_100a): RMSNorm (with the
+// residual add folded in), per-head q/k RMSNorm + rotary embedding + KV-cache
+// write, and grouped-query attention of one new token against the cache.
+//
+// The math is HF transformers' Qwen3 (models/qwen3: Qwen3RMSNorm,
+// apply_rotary_pos_emb with rotate_half, grouped-query attention with
+// softmax scale d^-1/2).  Element-wise steps round to the activation dtype at
+// the same points as the unfused torch sequence; reductions (sum of squares,
+// softmax, the attention-weighted sum) accumulate in fp32.
+#include "cbq_common.cuh"
+
+namespace {
+
+using namespace cbq;
+
+template <typename T> __device__ __forceinline__ float ld(const T *p, int64_t i) { return to_f32(p[i]); }
+template <typename T> __device__ __forceinline__ float rnd(float v) { return to_f32(from_f32<T>(v)); }
+
+template <int NT>
+__device__ __forceinline__ float block_sum(float v, float *red) {
+    v = warp_sum(v);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    float t = 0.f;
+    if (w == 0) {
+        t = l < NT / 32 ? red[l] : 0.f;
+        t = warp_sum(t);
+        if (l == 0) red[0] = t;
+    }
+    __syncthreads();
+    t = red[0];
+    __syncthreads();
+    return t;
+}
+
+// ------------------------------------------------------------------ RMSNorm
+// x[r] (+)= add[r] (rounded), out[r] = round(w * round(x * rsqrt(mean(x^2) + eps))).
+template <typename T, int NT>
+__global__ void __launch_bounds__(NT) k_rmsnorm(T *x, const T *add, int64_t n, const float *w, float eps,
+                                                T *out) {
+    __shared__ float red[32];
+    const int64_t r = blockIdx.x;
+    T *xr = x + r * n;
+    const T *ar = add ? add + r * n : nullptr;
+    T *orow = out + r * n;
+    float ss = 0.f;
+    for (int64_t i = threadIdx.x; i < n; i += NT) {
+        float v = ld(xr, i);
+        if (ar) {
+            v = rnd<T>(v + ld(ar, i));
+            xr[i] = from_f32<T>(v);
+        }
+        ss += v * v;
+    }
+    const float tot = block_sum<NT>(ss, red);
+    const float scale = rsqrtf(tot / (float)n + eps);
+    for (int64_t i = threadIdx.x; i < n; i += NT) {
+        float v = rnd<T>(ld(xr, i) * scale);
+        if (w) v = w[i] * v;
+        orow[i] = from_f32<T>(v);
+    }
+}
+
+// ------------------------------------------- q/k norm + rope + cache write
+// One warp per head: heads [0, Hq) of q, then Hkv of k, then Hkv of v, for
+// each of B rows.  Lane l holds elements [l*E, l*E + E) with E = d/32;
+// rotate_half's partner of element i is i +- d/2, held by lane l ^ 16.
+template <typename T, int E>
+__global__ void __launch_bounds__(256) k_qk_norm_rope(const T *q, const T *k, const T *v, int B, int Hq,
+                                                      int Hkv, float eps, const float *qw, const float *kw,
+                                                      const float *cosT, const float *sinT,
+                                                      const int64_t *pos_dev, T *q_out, T *k_cache,
+                                                      T *v_cache, int64_t L) {
+    constexpr int D = 32 * E;
+    const int gw = (int)((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5);
+    const int lane = threadIdx.x & 31;
+    const int per_row = Hq + 2 * Hkv;
+    if (gw >= B * per_row) return;
+    const int b = gw / per_row, h = gw - b * per_row;
+    const int64_t pos = *pos_dev;
+    if (pos < 0 || pos >= L) return;                  // outside the cache: write nothing
+    float x[E];
+    const T *src;
+    int kind, hh;
+    if (h < Hq) { kind = 0; hh = h; src = q + ((int64_t)b * Hq + hh) * D; }
+    else if (h < Hq + Hkv) { kind = 1; hh = h - Hq; src = k + ((int64_t)b * Hkv + hh) * D; }
+    else { kind = 2; hh = h - Hq - Hkv; src = v + ((int64_t)b * Hkv + hh) * D; }
+#pragma unroll
+    for (int e = 0; e < E; ++e) x[e] = ld(src, lane * E + e);
+    if (kind == 2) {
+        T *dst = v_cache + (((int64_t)b * Hkv + hh) * L + pos) * D;
+#pragma unroll
+        for (int e = 0; e < E; ++e) dst[lane * E + e] = from_f32<T>(x[e]);
+        return;
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) ss += x[e] * x[e];
+    ss = warp_sum(ss);
+    const float scale = rsqrtf(ss / (float)D + eps);
+    const float *wt = kind == 0 ? qw : kw;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        x[e] = rnd<T>(x[e] * scale);
+        if (wt) x[e] = rnd<T>(wt[lane * E + e] * x[e]);
+    }
+    const float *cr = cosT + pos * D, *sr = sinT + pos * D;
+    float o[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const int i = lane * E + e;
+        const float partner = __shfl_xor_sync(0xffffffffu, x[e], 16);
+        const float rot = i < D / 2 ? -partner : partner;
+        const float c = rnd<T>(cr[i]), s = rnd<T>(sr[i]);
+        o[e] = rnd<T>(rnd<T>(x[e] * c) + rnd<T>(rot * s));
+    }
+    T *dst = kind == 0 ? q_out + ((int64_t)b * Hq + hh) * D
+                       : k_cache + (((int64_t)b * Hkv + hh) * L + pos) * D;
+#pragma unroll
+    for (int e = 0; e < E; ++e) dst[lane * E + e] = from_f32<T>(o[e]);
+}
+
+// -------------------------------------------------------- decode attention
+// One CTA (D threads, D = head dim) per (row b, query head h): scores of keys
+// 0..pos, softmax, weighted sum of values, all in fp32.
+template <typename T, int D>
+__global__ void __launch_bounds__(D) k_attn_decode(const T *q, const T *k_cache, const T *v_cache,
+                                                   const int64_t *pos_dev, int Hq, int Hkv, int64_t L,
+                                                   float scale, T *out) {
+    constexpr int NW = D / 32, E = D / 32;
+    extern __shared__ float sc[];                 // scores [L]
+    __shared__ float red[32];
+    const int bh = blockIdx.x;
+    const int b = bh / Hq, h = bh - b * Hq;
+    const int g = h / (Hq / Hkv);
+    const int64_t n = min(*pos_dev + 1, L);            // keys 0..pos (none if pos < 0)
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const T *qr = q + ((int64_t)b * Hq + h) * D;
+    float qv[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) qv[e] = ld(qr, lane * E + e);
+    const T *kb = k_cache + ((int64_t)b * Hkv + g) * L * D;
+    const T *vb = v_cache + ((int64_t)b * Hkv + g) * L * D;
+    float mx = -INFINITY;
+    for (int64_t j = warp; j < n; j += NW) {
+        const T *kr = kb + j * D + lane * E;
+        float d = 0.f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) d += qv[e] * ld(kr, e);
+        d = warp_sum(d) * scale;
+        if (lane == 0) sc[j] = d;
+        mx = fmaxf(mx, d);
+    }
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) mx = fmaxf(mx, red[w]);
+    __syncthreads();
+    float sum = 0.f;
+    for (int64_t j = threadIdx.x; j < n; j += D) {
+        const float p = expf(sc[j] - mx);
+        sc[j] = p;
+        sum += p;
+    }
+    sum = block_sum<D>(sum, red);            // includes the barrier that publishes sc[]
+    if (n <= 0) {
+        out[((int64_t)b * Hq + h) * D + threadIdx.x] = from_f32<T>(0.f);
+        return;
+    }
+    float acc0 = 0.f, acc1 = 0.f;
+    const int i = threadIdx.x;
+    int64_t j = 0;
+    for (; j + 1 < n; j += 2) {
+        acc0 = fmaf(sc[j], ld(vb, j * D + i), acc0);
+        acc1 = fmaf(sc[j + 1], ld(vb, (j + 1) * D + i), acc1);
+    }
+    if (j < n) acc0 = fmaf(sc[j], ld(vb, j * D + i), acc0);
+    out[((int64_t)b * Hq + h) * D + i] = from_f32<T>((acc0 + acc1) / sum);
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------- C ABI
+
+extern "C" int cbq_rmsnorm(void *x_dev, const void *add_dev, int dtype, int64_t rows, int64_t n,
+                           const float *weight_dev, float eps, void *out_dev, void *stream) {
+    if (rows < 0 || n < 1 || (dtype != CBQ_F32 && dtype != CBQ_BF16)) return CBQ_ERR_ARG;
+    if (rows == 0) return CBQ_OK;
+    if (!x_dev || !out_dev || rows > 0x7fffffff) return CBQ_ERR_ARG;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (dtype == CBQ_F32)
+        k_rmsnorm<float, 256><<<(unsigned)rows, 256, 0, s>>>(static_cast<float *>(x_dev),
+                                                             static_cast<const float *>(add_dev), n,
+                                                             weight_dev, eps, static_cast<float *>(out_dev));
+    else
+        k_rmsnorm<__nv_bfloat16, 256><<<(unsigned)rows, 256, 0, s>>>(
+            static_cast<__nv_bfloat16 *>(x_dev), static_cast<const __nv_bfloat16 *>(add_dev), n, weight_dev,
+            eps, static_cast<__nv_bfloat16 *>(out_dev));
+    CBQ_CUDA_TRY(cudaGetLastError());
+    return CBQ_OK;
+}
+
+extern "C" int cbq_qk_norm_rope(const void *q_dev, const void *k_dev, const void *v_dev, int dtype, int64_t B,
+                                int64_t Hq, int64_t Hkv, int64_t head_dim, float eps, const float *q_weight_dev,
+                                const float *k_weight_dev, const float *cos_dev, const float *sin_dev,
+                                const int64_t *pos_dev, void *q_out_dev, void *k_cache_dev, void *v_cache_dev,
+                                int64_t cache_len, void *stream) {
+    if (B < 0 || Hq < 1 || Hkv < 1 || Hq % Hkv || (dtype != CBQ_F32 && dtype != CBQ_BF16)) return CBQ_ERR_ARG;
+    if (head_dim != 64 && head_dim != 128 && head_dim != 256) return CBQ_ERR_UNSUPPORTED;
+    if (B == 0) return CBQ_OK;
+    if (!q_dev || !k_dev || !v_dev || !cos_dev || !sin_dev || !pos_dev || !q_out_dev || !k_cache_dev ||
+        !v_cache_dev || cache_len < 1)
+        return CBQ_ERR_ARG;
+    const int64_t warps = B * (Hq + 2 * Hkv);
+    if (warps * 32 > 0x7fffffffll) return CBQ_ERR_ARG;
+    const unsigned grid = (unsigned)((warps * 32 + 255) / 256);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define CBQ_QK(T, E)                                                                               \
+    k_qk_norm_rope<T, E><<<grid, 256, 0, s>>>(                                                     \
+        static_cast<const T *>(q_dev), static_cast<const T *>(k_dev), static_cast<const T *>(v_dev), \
+        (int)B, (int)Hq, (int)Hkv, eps, q_weight_dev, k_weight_dev, cos_dev, sin_dev, pos_dev,      \
+        static_cast<T *>(q_out_dev), static_cast<T *>(k_cache_dev), static_cast<T *>(v_cache_dev),  \
+        cache_len)
+    if (dtype == CBQ_F32) {
+        if (head_dim == 64) CBQ_QK(float, 2); else if (head_dim == 128) CBQ_QK(float, 4); else CBQ_QK(float, 8);
+    } else {
+        if (head_dim == 64) CBQ_QK(__nv_bfloat16, 2);
+        else if (head_dim == 128) CBQ_QK(__nv_bfloat16, 4);
+        else CBQ_QK(__nv_bfloat16, 8);
+    }
+#undef CBQ_QK
+    CBQ_CUDA_TRY(cudaGetLastError());
+    return CBQ_OK;
+}
+
+extern "C" int cbq_attn_decode(const void *q_dev, const void *k_cache_dev, const void *v_cache_dev, int dtype,
+                               int64_t B, int64_t Hq, int64_t Hkv, int64_t head_dim, int64_t cache_len,
+                               const int64_t *pos_dev, float scale, void *out_dev, void *stream) {
+    if (B < 0 || Hq < 1 || Hkv < 1 || Hq % Hkv || cache_len < 1 || (dtype != CBQ_F32 && dtype != CBQ_BF16))
+        return CBQ_ERR_ARG;
+    if (head_dim != 64 && head_dim != 128 && head_dim != 256) return CBQ_ERR_UNSUPPORTED;
+    if (cache_len > 32768) return CBQ_ERR_UNSUPPORTED;           // scores live in shared memory
+    if (B == 0) return CBQ_OK;
+    if (!q_dev || !k_cache_dev || !v_cache_dev || !pos_dev || !out_dev || B * Hq > 0x7fffffff) return CBQ_ERR_ARG;
+    const size_t smem = (size_t)cache_len * 4;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define CBQ_AT(T, D)                                                                                 \
+    do {                                                                                             \
+        if (smem > 48 * 1024)                                                                        \
+            CBQ_CUDA_TRY(cudaFuncSetAttribute(k_attn_decode<T, D>,                                   \
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
+        k_attn_decode<T, D><<<(unsigned)(B * Hq), D, smem, s>>>(                                     \
+            static_cast<const T *>(q_dev), static_cast<const T *>(k_cache_dev),                      \
+            static_cast<const T *>(v_cache_dev), pos_dev, (int)Hq, (int)Hkv, cache_len, scale,       \
+            static_cast<T *>(out_dev));                                                              \
+    } while (0)
+    if (dtype == CBQ_F32) {
+        if (head_dim == 64) CBQ_AT(float, 64); else if (head_dim == 128) CBQ_AT(float, 128); else CBQ_AT(float, 256);
+    } else {
+        if (head_dim == 64) CBQ_AT(__nv_bfloat16, 64);
+        else if (head_dim == 128) CBQ_AT(__nv_bfloat16, 128);
+        else CBQ_AT(__nv_bfloat16, 256);
+    }
+#undef CBQ_AT
+    CBQ_CUDA_TRY(cudaGetLastError());
+    return CBQ_OK;
+}

@@ -140,11 +140,12 @@ struct GemvPlan {
     size_t smem = 0;
 };
 
-bool plan_gemv(int64_t M, int64_t K, int bits, int64_t C, int64_t T, GemvPlan &p) {
+bool plan_gemv(int64_t M, int64_t K, int bits, int64_t C, int64_t T, GemvPlan &p, bool even_rows = false) {
     if (T < 1 || T > 2 || K <= 0 || K % 128 != 0 || K > (1 << 20) || M <= 0 || M >= (1ll << 31))
         return false;
     const int64_t sms = cbq_host::sm_count();
-    const int64_t rows = (M + sms - 1) / sms;
+    int64_t rows = (M + sms - 1) / sms;
+    if (even_rows) rows += rows & 1;
     const int nseg = (int)((K + kGvSeg - 1) / kGvSeg);
     const int64_t NP = (bits <= 14) ? std::max<int64_t>(C, 1ll << bits) : C;
     const size_t budget = (size_t)cbq_host::max_smem_optin();
@@ -194,9 +195,11 @@ int linear_fixed_impl(const void *x, int x_dtype, int64_t T, int64_t ldx, const 
     GemvPlan g;
     if (aligned && x_aligned && plan_gemv(M, K, bits, C, T, g)) {
         GemvArgs a{};
-        a.x = x; a.ldx = ldx; a.t0 = 0; a.ntok = (int)T; a.packed = packed; a.codebook = cb;
+        a.x = x; a.ldx = ldx; a.t0 = 0; a.ntok = (int)T; a.codebook = cb;
         a.C = (int)C; a.M = (int)M; a.K = (int)K; a.nseg = g.nseg; a.rows_per_cta = g.rows_per_cta;
-        a.bias = bias; a.out = out; a.ldo = ldo; a.out_bf16 = out_dtype == CBQ_BF16;
+        a.nmat = 1; a.epi = kEpiStore;
+        a.mat[0] = GemvMat{packed, out, bias, nullptr, ldo, (int)M};
+        a.out_bf16 = out_dtype == CBQ_BF16;
         a.H = g.H; a.NP = g.NP; a.m128 = 128u; a.m4 = 4u; a.status = nullptr;
         return launch_gemv(bits, (int)T, x_dtype == CBQ_BF16, a, g.smem, g.grid, s);
     }
@@ -265,6 +268,48 @@ extern "C" int cbq_linear_fixed(const void *x_dev, int x_dtype, int64_t T, int64
     return linear_fixed_impl(x_dev, x_dtype, T, ldx, packed_dev, codebook_dev, C, bits, M, K,
                              bias_dev, out_dev, out_dtype, ldo, workspace_dev, workspace_bytes,
                              static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int cbq_linear_fixed_multi(const void *x_dev, int x_dtype, int64_t T, int64_t ldx, int nmat,
+                                      const uint8_t *const *packed_dev, const int64_t *packed_bytes,
+                                      const int64_t *M, const float *codebook_dev, int64_t C, int bits,
+                                      int64_t K, const float *const *bias_dev, void *const *out_dev,
+                                      const int64_t *ldo, const void *const *resid_dev, int out_dtype,
+                                      int epilogue, void *stream) {
+    if (nmat < 1 || nmat > kGvMaxMats || !packed_dev || !packed_bytes || !M || !out_dev || !ldo)
+        return CBQ_ERR_ARG;
+    if (T < 0 || K < 0 || bits < 1 || bits > 16 || C < 1 || C > 65536) return CBQ_ERR_ARG;
+    if ((x_dtype != CBQ_F32 && x_dtype != CBQ_BF16) || (out_dtype != CBQ_F32 && out_dtype != CBQ_BF16))
+        return CBQ_ERR_ARG;
+    if (epilogue != CBQ_EPI_STORE && epilogue != CBQ_EPI_RESIDUAL && epilogue != CBQ_EPI_SILU_MUL)
+        return CBQ_ERR_ARG;
+    if (epilogue == CBQ_EPI_SILU_MUL && (nmat != 2 || M[0] != M[1])) return CBQ_ERR_ARG;
+    if (epilogue == CBQ_EPI_RESIDUAL && !resid_dev) return CBQ_ERR_ARG;
+    int64_t Mt = 0;
+    for (int m = 0; m < nmat; ++m) {
+        if (M[m] < 1 || !packed_dev[m] || !out_dev[m] || ldo[m] < M[m]) return CBQ_ERR_ARG;
+        if (packed_bytes[m] < cbq_fixed_stream_bytes(M[m], K, bits)) return CBQ_ERR_ARG;
+        if ((reinterpret_cast<uintptr_t>(packed_dev[m]) & 15) != 0) return CBQ_ERR_UNSUPPORTED;
+        if (epilogue == CBQ_EPI_RESIDUAL && !resid_dev[m]) return CBQ_ERR_ARG;
+        Mt += M[m];
+    }
+    if (T == 0) return CBQ_OK;
+    if (!x_dev || !codebook_dev || ldx < K) return CBQ_ERR_ARG;
+    const int xbytes = x_dtype == CBQ_BF16 ? 2 : 4;
+    if ((reinterpret_cast<uintptr_t>(x_dev) & 15) != 0 || (ldx * xbytes) % 16 != 0) return CBQ_ERR_UNSUPPORTED;
+    GemvPlan g;
+    if (!plan_gemv(Mt, K, bits, C, T, g, epilogue == CBQ_EPI_SILU_MUL)) return CBQ_ERR_UNSUPPORTED;
+    GemvArgs a{};
+    a.x = x_dev; a.ldx = ldx; a.t0 = 0; a.ntok = (int)T; a.codebook = codebook_dev;
+    a.C = (int)C; a.M = (int)Mt; a.K = (int)K; a.nseg = g.nseg; a.rows_per_cta = g.rows_per_cta;
+    a.nmat = nmat; a.epi = epilogue;
+    for (int m = 0; m < nmat; ++m)
+        a.mat[m] = GemvMat{packed_dev[m], out_dev[m], bias_dev ? bias_dev[m] : nullptr,
+                           resid_dev ? resid_dev[m] : nullptr, ldo[m], (int)M[m]};
+    a.out_bf16 = out_dtype == CBQ_BF16;
+    a.H = g.H; a.NP = g.NP; a.m128 = 128u; a.m4 = 4u; a.status = nullptr;
+    return launch_gemv(bits, (int)T, x_dtype == CBQ_BF16, a, g.smem, g.grid,
+                       static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int cbq_embedding_fixed(const int64_t *ids_dev, int64_t T, const uint8_t *packed_dev,

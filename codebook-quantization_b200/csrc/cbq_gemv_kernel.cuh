@@ -48,25 +48,58 @@ constexpr int kGvSlots = CBQ_GV_SLOTS;   // ring slots per warp
 constexpr size_t kGvBarBytes = a128((size_t)kGvWarps * kGvSlots * 8);   // one mbarrier per slot
 static_assert(kGvWarps * 32 <= 1024 && kGvSlots >= 2, "gemv launch shape");
 
+constexpr int kGvMaxMats = 3;
+
+// One matrix of a launch.  Several matrices that share K, the bit width, the
+// codebook and the activations (q/k/v, gate/up) are decoded by one launch.
+struct GemvMat {
+    const uint8_t *packed;
+    void *out;           // [T, ldo] in the output dtype
+    const float *bias;   // [M] or null
+    const void *resid;   // EPI_RESIDUAL: [T, ldo] in the output dtype (may alias out)
+    int64_t ldo;
+    int M;
+};
+
+enum GemvEpi : int {
+    kEpiStore = 0,       // out = acc (+ bias)
+    kEpiResidual = 1,    // out = resid + round(acc + bias)      (the residual stream update)
+    kEpiSiluMul = 2,     // two matrices of equal M: out0 = round(silu(round(g)) * round(u))
+};
+
 struct GemvArgs {
     const void *x;
     int64_t ldx;
     int64_t t0;          // first token of this launch
     int ntok;            // tokens in this launch (<= TB)
-    const uint8_t *packed;
     const float *codebook;
     int C;
-    int M, K, nseg;
+    int M, K, nseg;      // M: rows of all matrices (the launch's row space)
     int rows_per_cta;
-    const float *bias;
-    void *out;
-    int64_t ldo;
+    int nmat;
+    int epi;             // GemvEpi; kEpiSiluMul interleaves the two matrices' rows
+    GemvMat mat[kGvMaxMats];
     int out_bf16;
     uint32_t H;          // replicated codebook entries
     uint32_t NP;         // entries held in shared memory (head + single copy)
     uint32_t m128, m4;   // 128 and 4
     uint32_t *status;
 };
+
+// Row v of the launch's row space -> (matrix, row of that matrix).  Rows are
+// the matrices' rows one after another, or (kEpiSiluMul) interleaved so that
+// row r of both matrices lands in the same CTA.
+__device__ __forceinline__ int gv_locate(const GemvArgs &a, int64_t v, int64_t &row) {
+    if (a.epi == kEpiSiluMul) {
+        row = v >> 1;
+        return (int)(v & 1);
+    }
+    int m = 0;
+    int64_t base = 0;
+    while (m + 1 < a.nmat && v >= base + a.mat[m].M) base += a.mat[m++].M;
+    row = v - base;
+    return m;
+}
 
 // Shared-memory layout: [barriers][row-segment sums][codebook][rings].
 __host__ __device__ inline size_t gemv_part_bytes(int rows_per_cta, int nseg, int TB) {
@@ -175,9 +208,11 @@ __global__ void __launch_bounds__(kGvWarps * 32, 1) k_gemv_fixed(const GemvArgs 
     auto issue_next = [&]() {                                // lane 0 only
         const int cnt = min(kGvSeg, K - is * kGvSeg);
         const uint32_t bytes = (uint32_t)cnt * BITS / 8;
+        int64_t row;
+        const int m = gv_locate(a, m0 + irl, row);
         mbar_arrive_expect_tx(&bars[islot], bytes);
         bulk_g2s(ring + (size_t)islot * kSegBytes,
-                 a.packed + ((m0 + irl) * (int64_t)K + (int64_t)is * kGvSeg) * BITS / 8, bytes,
+                 a.mat[m].packed + (row * (int64_t)K + (int64_t)is * kGvSeg) * BITS / 8, bytes,
                  &bars[islot]);
         if (++irl == nrows) { irl = 0; ++is; }
         if (++islot == kGvSlots) islot = 0;
@@ -338,15 +373,46 @@ __global__ void __launch_bounds__(kGvWarps * 32, 1) k_gemv_fixed(const GemvArgs 
     }
     __syncthreads();
 
-    // rows: segment sums in segment order, + bias, in the output dtype
-    for (int r = tid; r < nrows; r += kGvWarps * 32) {
-        const float b = a.bias ? a.bias[m0 + r] : 0.f;
-        for (int t = 0; t < a.ntok; ++t) {
-            float sum = 0.f;
-            for (int q = 0; q < nseg; ++q) sum += part[((size_t)r * nseg + q) * TB + t];
-            const int64_t o = (a.t0 + t) * a.ldo + m0 + r;
-            if (a.out_bf16) static_cast<__nv_bfloat16 *>(a.out)[o] = __float2bfloat16_rn(sum + b);
-            else static_cast<float *>(a.out)[o] = sum + b;
+    // rows: segment sums in segment order, + bias, then the epilogue, in the
+    // output dtype.  Intermediate roundings follow the unfused sequence of
+    // operations (linear output rounded, then the add / SiLU / product
+    // rounded), so fused and unfused decoders compute the same values.
+    auto seg_sum = [&](int r, int t) {
+        float sum = 0.f;
+        for (int q = 0; q < nseg; ++q) sum += part[((size_t)r * nseg + q) * TB + t];
+        return sum;
+    };
+    auto rnd = [&](float v) { return a.out_bf16 ? __bfloat162float(__float2bfloat16_rn(v)) : v; };
+    auto store = [&](const GemvMat &mt, int64_t o, float v) {
+        if (a.out_bf16) static_cast<__nv_bfloat16 *>(mt.out)[o] = __float2bfloat16_rn(v);
+        else static_cast<float *>(mt.out)[o] = v;
+    };
+    auto load = [&](const void *p, int64_t o) {
+        return a.out_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16 *>(p)[o])
+                          : static_cast<const float *>(p)[o];
+    };
+    if (a.epi == kEpiSiluMul) {
+        const GemvMat &g = a.mat[0], &u = a.mat[1];
+        for (int r = 2 * tid; r + 1 < nrows; r += 2 * kGvWarps * 32) {
+            const int64_t row = (m0 + r) >> 1;
+            const float bg = g.bias ? g.bias[row] : 0.f, bu = u.bias ? u.bias[row] : 0.f;
+            for (int t = 0; t < a.ntok; ++t) {
+                const float gv = rnd(seg_sum(r, t) + bg), uv = rnd(seg_sum(r + 1, t) + bu);
+                const float sv = rnd(gv / (1.0f + expf(-gv)));
+                store(g, (a.t0 + t) * g.ldo + row, sv * uv);
+            }
+        }
+    } else {
+        for (int r = tid; r < nrows; r += kGvWarps * 32) {
+            int64_t row;
+            const GemvMat &mt = a.mat[gv_locate(a, m0 + r, row)];
+            const float b = mt.bias ? mt.bias[row] : 0.f;
+            for (int t = 0; t < a.ntok; ++t) {
+                const int64_t o = (a.t0 + t) * mt.ldo + row;
+                float v = seg_sum(r, t) + b;
+                if (a.epi == kEpiResidual) v = load(mt.resid, o) + rnd(v);
+                store(mt, o, v);
+            }
         }
     }
 }

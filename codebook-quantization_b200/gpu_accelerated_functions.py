@@ -20,7 +20,8 @@ import torch
 
 from . import _lib
 
-__all__ = ["GPUAcceleratedLinear", "GPUAcceleratedEmbedding", "device_stream", "as_kernel_input"]
+__all__ = ["GPUAcceleratedLinear", "GPUAcceleratedEmbedding", "device_stream", "as_kernel_input",
+           "linear_fixed_multi"]
 
 
 def device_stream(device: torch.device) -> int:
@@ -156,6 +157,47 @@ class GPUAcceleratedLinear:
         return res if res.dtype == want else res.to(want)
 
 
+def linear_fixed_multi(mats, x: torch.Tensor, outs, epilogue: int = 0, resids=None) -> bool:
+    """One launch of ``cbq_linear_fixed_multi`` over ``mats`` (GPUAcceleratedLinear
+    objects sharing K, bits and codebook) for ``x [T, K]``.  ``outs[i]`` are
+    ``[T, M_i]`` tensors (for ``CBQ_EPI_SILU_MUL`` only ``outs[0]`` is
+    written); ``resids[i]`` the residual inputs of ``CBQ_EPI_RESIDUAL`` (may be
+    ``outs[i]`` itself).  Returns False, having launched nothing, when the
+    shape is outside what the fused kernel supports (T > 2, unaligned rows);
+    the caller then runs the matrices one by one."""
+    import ctypes as ct
+    n = len(mats)
+    m0 = mats[0]
+    if any(m.K != m0.K or m.bits != m0.bits or m.codebook.data_ptr() != m0.codebook.data_ptr()
+           or m.device != m0.device for m in mats):
+        raise ValueError("linear_fixed_multi: matrices must share K, bits, codebook and device")
+    x2, xcode = as_kernel_input(x, m0.K)
+    T = x2.shape[0]
+    outs = list(outs)
+    if epilogue == _lib.CBQ_EPI_SILU_MUL:
+        outs = outs[:1] * n                  # both rows of a pair land in outs[0]
+    if len(outs) != n:
+        raise ValueError(f"linear_fixed_multi: {n} matrices but {len(outs)} outputs")
+    odt = outs[0].dtype
+    ocode = _lib.CBQ_BF16 if odt == torch.bfloat16 else _lib.CBQ_F32
+    P, I64 = ct.c_void_p, ct.c_int64
+    packed = (P * n)(*[m.packed.data_ptr() for m in mats])
+    nbytes = (I64 * n)(*[m.nbytes for m in mats])
+    Ms = (I64 * n)(*[m.M for m in mats])
+    optrs = (P * n)(*[o.data_ptr() for o in outs])
+    ldo = (I64 * n)(*[o.stride(0) if o.dim() > 1 and T > 1 else o.shape[-1] for o in outs])
+    rp = None if resids is None else (P * n)(*[r.data_ptr() for r in resids])
+    rc = _lib.lib().cbq_linear_fixed_multi(
+        x2.data_ptr(), xcode, T, x2.stride(0) if T > 1 else m0.K, n, packed, nbytes, Ms,
+        m0.codebook.data_ptr(), m0.C, m0.bits, m0.K, None, optrs, ldo, rp, ocode, int(epilogue),
+        device_stream(m0.device))
+    if rc == _lib.CBQ_ERR_UNSUPPORTED:
+        return False
+    if rc != _lib.CBQ_OK:
+        raise _lib.CbqError("cbq_linear_fixed_multi", rc)
+    return True
+
+
 class GPUAcceleratedEmbedding:
     """Packed fixed-width embedding table on the GPU; ``__call__(ids)`` decodes
     only the requested rows (``src/gpu_accelerated_functions.py:109-126``)."""
@@ -176,12 +218,16 @@ class GPUAcceleratedEmbedding:
                                           self.device)
         self.status = torch.tensor([0, -1, 0, 0], dtype=torch.int32, device=self.device)
 
-    def __call__(self, ids: torch.Tensor, out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    def __call__(self, ids: torch.Tensor, out_dtype: torch.dtype = torch.float32,
+                 out: torch.Tensor = None) -> torch.Tensor:
         lead = ids.shape
         flat = ids.reshape(-1).to(device=self.device, dtype=torch.int64).contiguous()
         T = flat.numel()
+        if out is not None:
+            out_dtype = out.dtype
         kdt = out_dtype if out_dtype in (torch.float32, torch.bfloat16) else torch.float32
-        out = torch.empty((T, self.hidden), dtype=kdt, device=self.device)
+        if out is None or out.dtype != kdt or not out.is_contiguous():
+            out = torch.empty((T, self.hidden), dtype=kdt, device=self.device)
         _lib.call("cbq_embedding_fixed", flat.data_ptr(), T, self.packed.data_ptr(), self.nbytes,
                   self.codebook.data_ptr(), self.C, self.bits, self.vocab, self.hidden,
                   out.data_ptr(), _lib.CBQ_BF16 if kdt == torch.bfloat16 else _lib.CBQ_F32,

@@ -207,12 +207,16 @@ class HuffmanCodebookEmbedding:
                                 huff_row_bit_starts, self.device)
         self.status = self.hs.status
 
-    def __call__(self, ids: torch.Tensor, out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    def __call__(self, ids: torch.Tensor, out_dtype: torch.dtype = torch.float32,
+                 out: torch.Tensor = None) -> torch.Tensor:
         lead = ids.shape
         flat = ids.reshape(-1).to(device=self.device, dtype=torch.int64).contiguous()
         T = flat.numel()
+        if out is not None:
+            out_dtype = out.dtype
         kdt = out_dtype if out_dtype in (torch.float32, torch.bfloat16) else torch.float32
-        out = torch.empty((T, self.hidden), dtype=kdt, device=self.device)
+        if out is None or out.dtype != kdt or not out.is_contiguous():
+            out = torch.empty((T, self.hidden), dtype=kdt, device=self.device)
         hs = self.hs
         _lib.call("cbq_embedding_huff", flat.data_ptr(), T, hs.stream.data_ptr(), hs.nbytes,
                   hs.tables.data_ptr(), hs.rbs.data_ptr(), hs.chunk.data_ptr(), self.codebook.data_ptr(),

@@ -15,6 +15,17 @@ in a CUDA graph and replayed for every prompt and generated token with no host
 synchronisation.  Under tensor parallelism (``group`` given) heads and MLP
 columns are split per rank, o_proj/down_proj partial sums are all-reduced over
 NCCL, and the greedy argmax combines each rank's (max, index) pair.
+
+Two step implementations compute the same function:
+
+* ``fused=True`` (default): eight ``libcbq`` launches per layer -- one
+  decode-GEMV launch for q/k/v, q/k RMSNorm + rotary + cache write, decode
+  attention, o_proj with the residual add fused, RMSNorm, one launch for
+  gate/up with SiLU(gate)*up fused, down_proj with the residual add fused,
+  RMSNorm (under tensor parallelism the residual adds move into the RMSNorm
+  launch, after the all-reduce);
+* ``fused=False``: the same layer written with torch operations around one
+  ``libcbq`` launch per linear layer (about fifty launches per layer).
 """
 from __future__ import annotations
 
@@ -24,6 +35,8 @@ import torch
 import torch.distributed as dist
 import torch.nn.functional as F
 
+from . import _lib
+from .gpu_accelerated_functions import GPUAcceleratedLinear, device_stream, linear_fixed_multi
 from .qwen3 import CompressedQwen3Weights
 
 __all__ = ["Qwen3Decoder", "rope_tables"]
@@ -53,7 +66,7 @@ def _rms(x, eps):
 
 class Qwen3Decoder:
     def __init__(self, weights: CompressedQwen3Weights, batch: int, max_len: int,
-                 act_dtype=torch.bfloat16, group: Optional[dist.ProcessGroup] = None):
+                 act_dtype=torch.bfloat16, group: Optional[dist.ProcessGroup] = None, fused: bool = True):
         self.w, self.cfg = weights, weights.cfg
         cfg = self.cfg
         self.dev = weights.device
@@ -77,6 +90,15 @@ class Qwen3Decoder:
         self.graph = None
         self.vocab_local = cfg.vocab // self.world
         self.ar = torch.arange(max_len, device=self.dev)
+        self.fused = fused
+        if fused:
+            hq, hkv = self.hl * d, self.kvl * d
+            z = lambda n: torch.zeros(batch, n, dtype=act_dtype, device=self.dev)
+            self.x, self.h, self.y = z(cfg.hidden), z(cfg.hidden), z(cfg.hidden)
+            self.q, self.k, self.v = z(hq), z(hkv), z(hkv)
+            self.qn, self.a = z(hq), z(hq)
+            self.m = z(cfg.inter // self.world)
+            self.code = _lib.CBQ_BF16 if act_dtype == torch.bfloat16 else _lib.CBQ_F32
         L = weights.layers
         self.emb = L["model.embed_tokens.weight"]
         self.lm_head = L["lm_head.weight"]
@@ -94,6 +116,8 @@ class Qwen3Decoder:
         return t
 
     def _step(self):
+        if self.fused:
+            return self._step_fused()
         cfg, B, d, eps, dt = self.cfg, self.B, self.cfg.head_dim, self.cfg.rms_eps, self.dt
         x = self.emb(self.ids, out_dtype=dt)                         # [B, H]
         cos = self.cos.index_select(0, self.pos).to(dt)              # [1, d]
@@ -113,7 +137,62 @@ class Qwen3Decoder:
             x = x + self._allreduce(o_p(a.reshape(B, self.hl * d)))
             h = _rms(x, eps)
             x = x + self._allreduce(d_p(F.silu(g_p(h)) * u_p(h)))
-        logits = self.lm_head(_rms(x, eps))                          # [B, V / world]
+        self._finish(self.lm_head(_rms(x, eps)))                    # logits [B, V / world]
+
+    # ------------------------------------------------------------ fused step
+    def _rmsnorm(self, x, out, add=None):
+        _lib.call("cbq_rmsnorm", x.data_ptr(), None if add is None else add.data_ptr(), self.code,
+                  x.shape[0], x.shape[1], None, float(self.cfg.rms_eps), out.data_ptr(),
+                  device_stream(self.dev))
+
+    def _linear(self, mats, outs, epilogue=_lib.CBQ_EPI_STORE, resids=None, x=None):
+        x = self.h if x is None else x
+        fixed = all(isinstance(m, GPUAcceleratedLinear) for m in mats)
+        if fixed and linear_fixed_multi(mats, x, outs, epilogue, resids):
+            return
+        # matrices one by one (Huffman streams, or shapes outside the fused kernel)
+        if epilogue == _lib.CBQ_EPI_SILU_MUL:
+            g, u = mats[0](x), mats[1](x)
+            outs[0].copy_(F.silu(g) * u)
+        elif epilogue == _lib.CBQ_EPI_RESIDUAL:
+            for m, o, r in zip(mats, outs, resids):
+                o.copy_(r + m(x))
+        else:
+            for m, o in zip(mats, outs):
+                m(x, out=o)
+
+    def _step_fused(self):
+        cfg, B, d, dt = self.cfg, self.B, self.cfg.head_dim, self.dt
+        stream = device_stream(self.dev)
+        self.emb(self.ids, out=self.x)
+        self._rmsnorm(self.x, self.h)
+        for li, (q_p, k_p, v_p, o_p, g_p, u_p, d_p) in enumerate(self.layer_mods):
+            self._linear((q_p, k_p, v_p), (self.q, self.k, self.v))
+            _lib.call("cbq_qk_norm_rope", self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(), self.code,
+                      B, self.hl, self.kvl, d, float(cfg.rms_eps), None, None, self.cos.data_ptr(),
+                      self.sin.data_ptr(), self.pos.data_ptr(), self.qn.data_ptr(),
+                      self.k_cache[li].data_ptr(), self.v_cache[li].data_ptr(), self.max_len, stream)
+            _lib.call("cbq_attn_decode", self.qn.data_ptr(), self.k_cache[li].data_ptr(),
+                      self.v_cache[li].data_ptr(), self.code, B, self.hl, self.kvl, d, self.max_len,
+                      self.pos.data_ptr(), float(d ** -0.5), self.a.data_ptr(), stream)
+            if self.world == 1:
+                self._linear((o_p,), (self.x,), _lib.CBQ_EPI_RESIDUAL, (self.x,), x=self.a)
+                self._rmsnorm(self.x, self.h)
+            else:
+                self._linear((o_p,), (self.y,), x=self.a)
+                self._allreduce(self.y)
+                self._rmsnorm(self.x, self.h, add=self.y)
+            self._linear((g_p, u_p), (self.m,), _lib.CBQ_EPI_SILU_MUL)
+            if self.world == 1:
+                self._linear((d_p,), (self.x,), _lib.CBQ_EPI_RESIDUAL, (self.x,), x=self.m)
+                self._rmsnorm(self.x, self.h)
+            else:
+                self._linear((d_p,), (self.y,), x=self.m)
+                self._allreduce(self.y)
+                self._rmsnorm(self.x, self.h, add=self.y)
+        self._finish(self.lm_head(self.h))
+
+    def _finish(self, logits):
         self.logits = logits
         val, idx = logits.float().max(dim=-1)
         idx = idx + self.rank * self.vocab_local
@@ -125,6 +204,13 @@ class Qwen3Decoder:
             best = torch.stack(vals).max(dim=0).indices              # first rank on ties
             idx = torch.stack(idxs).gather(0, best.unsqueeze(0)).squeeze(0)
         self.next_ids.copy_(idx)
+
+    def launches_per_step(self) -> int:
+        """libcbq kernel launches in one step (embedding, linears, fused block kernels)."""
+        n = self.cfg.layers
+        if self.fused:
+            return 2 + 8 * n + 1          # embedding + first RMSNorm, 8 per layer, lm_head
+        return 1 + 7 * n + 1              # embedding, 7 linears per layer, lm_head
 
     def step(self, ids: torch.Tensor, pos: int) -> torch.Tensor:
         """Eager step (no graph): returns the greedy next ids [B]."""

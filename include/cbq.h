@@ -105,6 +105,31 @@ int cbq_linear_fixed(const void *x_dev, int x_dtype, int64_t T, int64_t ldx,
                      void *out_dev, int out_dtype, int64_t ldo,
                      void *workspace_dev, int64_t workspace_bytes, void *stream);
 
+/* Epilogues of cbq_linear_fixed_multi. */
+#define CBQ_EPI_STORE     0   /* out[m] = x @ W[m]^T (+ bias[m]) */
+#define CBQ_EPI_RESIDUAL  1   /* out[m] = resid[m] + round(x @ W[m]^T (+ bias[m])); resid may alias out */
+#define CBQ_EPI_SILU_MUL  2   /* nmat == 2, equal M: out[0] = round(silu(round(x@W0^T)) * round(x@W1^T)) */
+
+/* Several fixed-width matrices that share the activations, K, the bit width
+ * and the codebook, decoded by one launch (for example q/k/v, or gate/up),
+ * with an optional fused epilogue.  `round` is the rounding to out_dtype, so
+ * each epilogue gives the same values as the separate operations: the
+ * residual update `x + linear(h)` and the SiLU-gated product
+ * `silu(gate(h)) * up(h)` of a transformer block (HF Qwen3 MLP).  No
+ * counterpart in the reference, which launches one kernel per linear layer
+ * (src/gpu_accelerated_functions.py:238-274) and does the rest in torch.
+ * Host arrays (nmat entries): packed_dev, packed_bytes, M, bias_dev (array
+ * may be NULL), out_dev, ldo, resid_dev (CBQ_EPI_RESIDUAL only).
+ * Supports T <= 2 with 16-byte aligned x rows and streams, K % 128 == 0;
+ * anything else returns CBQ_ERR_UNSUPPORTED before launching (the caller then
+ * uses cbq_linear_fixed per matrix). */
+int cbq_linear_fixed_multi(const void *x_dev, int x_dtype, int64_t T, int64_t ldx, int nmat,
+                           const uint8_t *const *packed_dev, const int64_t *packed_bytes,
+                           const int64_t *M, const float *codebook_dev, int64_t C, int bits,
+                           int64_t K, const float *const *bias_dev, void *const *out_dev,
+                           const int64_t *ldo, const void *const *resid_dev, int out_dtype,
+                           int epilogue, void *stream);
+
 /* Size of the device array built into the library that
  * cbq_linear_fixed_noalloc uses as its workspace (8 MiB on every GPU that
  * loads the library, until the process exits). */
@@ -233,6 +258,43 @@ int cbq_huff_decode_indices(const uint8_t *stream_dev, int64_t stream_bytes,
 int cbq_huff_encode(const uint16_t *idx_dev, int64_t n, const uint32_t *code_dev,
                     const uint8_t *len_dev, const int64_t *bit_starts_dev,
                     uint8_t *out_dev, int64_t out_bytes, void *stream);
+
+/* ======================================================================
+ * Decode-step kernels around the compressed linear layers (one new token
+ * per sequence).  The math of HF transformers' Qwen3 decoder layer
+ * (models/qwen3); element-wise steps round to the activation dtype where the
+ * unfused sequence of torch operations does, reductions run in fp32.  No
+ * counterpart in the reference, which runs these steps through HF's torch
+ * modules (src/model_loader.py builds the HF model around the compressed
+ * linears).  dtype: CBQ_F32 or CBQ_BF16 for every activation and cache.
+ * ====================================================================== */
+
+/* Per row r of x [rows, n]: if add_dev, x[r] = round(x[r] + add[r]) (written
+ * back: the residual-stream update); then
+ * out[r] = round(w * round(x[r] * rsqrt(mean(x[r]^2) + eps))), w = weight_dev
+ * (fp32 [n]) or 1. */
+int cbq_rmsnorm(void *x_dev, const void *add_dev, int dtype, int64_t rows, int64_t n,
+                const float *weight_dev, float eps, void *out_dev, void *stream);
+
+/* The attention block's element-wise part for the token at position *pos_dev
+ * (device int64): per-head RMSNorm of q [B, Hq*d] and k [B, Hkv*d] (weights
+ * fp32 [d] or NULL = 1), rotary embedding with cos/sin tables (fp32
+ * [cache_len, d], rotate_half form), q -> q_out [B, Hq, d], k and v [B, Hkv*d]
+ * -> row *pos_dev of k_cache / v_cache [B, Hkv, cache_len, d].  head_dim 64,
+ * 128 or 256.  Nothing is written when *pos_dev is outside [0, cache_len). */
+int cbq_qk_norm_rope(const void *q_dev, const void *k_dev, const void *v_dev, int dtype, int64_t B,
+                     int64_t Hq, int64_t Hkv, int64_t head_dim, float eps, const float *q_weight_dev,
+                     const float *k_weight_dev, const float *cos_dev, const float *sin_dev,
+                     const int64_t *pos_dev, void *q_out_dev, void *k_cache_dev, void *v_cache_dev,
+                     int64_t cache_len, void *stream);
+
+/* Grouped-query attention of q [B, Hq, d] over cache rows 0..*pos_dev of
+ * k_cache / v_cache [B, Hkv, cache_len, d] (query head h reads kv head
+ * h / (Hq / Hkv)), softmax(q k^T * scale) v in fp32 -> out [B, Hq*d].
+ * cache_len <= 32768. */
+int cbq_attn_decode(const void *q_dev, const void *k_cache_dev, const void *v_cache_dev, int dtype,
+                    int64_t B, int64_t Hq, int64_t Hkv, int64_t head_dim, int64_t cache_len,
+                    const int64_t *pos_dev, float scale, void *out_dev, void *stream);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,168 @@
+"""Decode-step kernels: the multi-matrix decode-GEMV with its fused epilogues,
+RMSNorm, q/k RMSNorm + rotary + cache write, and decode attention.
+
+The multi-matrix launch is checked bit for bit against one cbq_linear_fixed
+call per matrix followed by the torch operations its epilogue replaces (the
+per-row sums are computed identically and the epilogue rounds where torch
+does).  The other kernels are checked against the torch formulation of HF
+Qwen3 within fp32 / bf16 tolerances (their reductions run in a different
+order from torch's).
+"""
+import importlib
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from helpers import cbq, need_cuda, rel_l2
+
+pytestmark = pytest.mark.gpu
+L = cbq._lib
+G = cbq.gpu_accelerated_functions
+
+
+def _mats(dev, Ms, K, bits=13, seed=0):
+    rng = np.random.default_rng(seed)
+    C = (1 << bits) - 5
+    cb = torch.from_numpy((rng.standard_normal(C) * 0.02).astype(np.float32)).to(dev)
+    mats = []
+    for i, M in enumerate(Ms):
+        idx = rng.integers(0, 1 << bits, size=M * K).astype(np.uint16)   # some >= C: clamped
+        mats.append(G.GPUAcceleratedLinear(f"m{i}", cbq.bitpack.pack_any_bits(idx, bits), cb, (M, K), bits,
+                                           device=dev))
+    return mats
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+@pytest.mark.parametrize("T", [1, 2])
+def test_multi_store_matches_single_calls(dt, T):
+    dev = need_cuda()
+    mats = _mats(dev, [512, 128, 128], 1024)
+    x = torch.randn(T, 1024, device=dev).to(dt)
+    outs = [torch.empty(T, m.M, device=dev, dtype=dt) for m in mats]
+    assert G.linear_fixed_multi(mats, x, outs)
+    for m, o in zip(mats, outs):
+        assert torch.equal(o, m(x)), m.name
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+def test_multi_residual_epilogue_is_the_torch_add(dt):
+    dev = need_cuda()
+    (m,) = _mats(dev, [2048], 4096, seed=1)
+    h = torch.randn(2, 4096, device=dev).to(dt)
+    x = torch.randn(2, 2048, device=dev).to(dt)
+    want = x + m(h)
+    got = x.clone()
+    assert G.linear_fixed_multi([m], h, [got], L.CBQ_EPI_RESIDUAL, [got])
+    assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+@pytest.mark.parametrize("M", [1536, 770])
+def test_multi_silu_mul_epilogue_is_the_torch_mlp(dt, M):
+    dev = need_cuda()
+    g, u = _mats(dev, [M, M], 2048, seed=2)
+    h = torch.randn(1, 2048, device=dev).to(dt)
+    want = F.silu(g(h)) * u(h)
+    got = torch.empty(1, M, device=dev, dtype=dt)
+    assert G.linear_fixed_multi([g, u], h, [got], L.CBQ_EPI_SILU_MUL)
+    assert torch.equal(got, want)
+
+
+def test_multi_declines_three_tokens():
+    dev = need_cuda()
+    mats = _mats(dev, [256], 1024)
+    x = torch.randn(3, 1024, device=dev)
+    out = torch.full((3, 256), 7.0, device=dev)
+    assert not G.linear_fixed_multi(mats, x, [out])
+    assert bool((out == 7.0).all())
+
+
+def _rms_ref(x, eps):
+    x32 = x.float()
+    return (x32 * torch.rsqrt(x32.pow(2).mean(-1, keepdim=True) + eps)).to(x.dtype)
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+def test_rmsnorm_with_and_without_residual_add(dt):
+    dev = need_cuda()
+    x = torch.randn(3, 4096, device=dev).to(dt)
+    y = torch.randn(3, 4096, device=dev).to(dt)
+    out = torch.empty_like(x)
+    code = L.CBQ_BF16 if dt == torch.bfloat16 else L.CBQ_F32
+    s = torch.cuda.current_stream(dev).cuda_stream
+    x0 = x.clone()
+    L.call("cbq_rmsnorm", x.data_ptr(), None, code, 3, 4096, None, 1e-6, out.data_ptr(), s)
+    assert torch.equal(x, x0)
+    tol = 1e-6 if dt == torch.float32 else 8e-3
+    assert rel_l2(out.float().cpu().numpy(), _rms_ref(x0, 1e-6).float().cpu().numpy()) < tol
+    L.call("cbq_rmsnorm", x.data_ptr(), y.data_ptr(), code, 3, 4096, None, 1e-6, out.data_ptr(), s)
+    assert torch.equal(x, x0 + y)                                  # the residual update, rounded like torch
+    assert rel_l2(out.float().cpu().numpy(), _rms_ref(x0 + y, 1e-6).float().cpu().numpy()) < tol
+
+
+def _rotate_half(x):
+    h = x.shape[-1] // 2
+    return torch.cat((-x[..., h:], x[..., :h]), dim=-1)
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+@pytest.mark.parametrize("d", [64, 128])
+def test_qk_norm_rope_and_cache_write(dt, d):
+    dev = need_cuda()
+    qd = importlib.import_module("codebook-quantization_b200.qwen3_decode")
+    B, Hq, Hkv, Lc, pos = 2, 8, 2, 20, 13
+    cos, sin = qd.rope_tables(d, Lc, 1e6, dev)
+    q = torch.randn(B, Hq * d, device=dev).to(dt)
+    k = torch.randn(B, Hkv * d, device=dev).to(dt)
+    v = torch.randn(B, Hkv * d, device=dev).to(dt)
+    q_out = torch.empty(B, Hq, d, device=dev, dtype=dt)
+    kc = torch.zeros(B, Hkv, Lc, d, device=dev, dtype=dt)
+    vc = torch.zeros_like(kc)
+    p = torch.tensor([pos], device=dev)
+    code = L.CBQ_BF16 if dt == torch.bfloat16 else L.CBQ_F32
+    L.call("cbq_qk_norm_rope", q.data_ptr(), k.data_ptr(), v.data_ptr(), code, B, Hq, Hkv, d, 1e-6, None, None,
+           cos.data_ptr(), sin.data_ptr(), p.data_ptr(), q_out.data_ptr(), kc.data_ptr(), vc.data_ptr(), Lc,
+           torch.cuda.current_stream(dev).cuda_stream)
+    c, s_ = cos[pos].to(dt), sin[pos].to(dt)
+    qn = _rms_ref(q.view(B, Hq, d), 1e-6)
+    kn = _rms_ref(k.view(B, Hkv, d), 1e-6)
+    q_ref = qn * c + _rotate_half(qn) * s_
+    k_ref = kn * c + _rotate_half(kn) * s_
+    tol = 1e-6 if dt == torch.float32 else 8e-3
+    assert rel_l2(q_out.float().cpu().numpy(), q_ref.float().cpu().numpy()) < tol
+    assert rel_l2(kc[:, :, pos].float().cpu().numpy(), k_ref.float().cpu().numpy()) < tol
+    assert torch.equal(vc[:, :, pos], v.view(B, Hkv, d))
+    others = torch.ones(Lc, dtype=torch.bool)
+    others[pos] = False
+    assert not bool(kc[:, :, others].any()) and not bool(vc[:, :, others].any())
+    # a position outside the cache writes nothing
+    p.fill_(Lc)
+    kc2 = kc.clone()
+    L.call("cbq_qk_norm_rope", q.data_ptr(), k.data_ptr(), v.data_ptr(), code, B, Hq, Hkv, d, 1e-6, None, None,
+           cos.data_ptr(), sin.data_ptr(), p.data_ptr(), q_out.data_ptr(), kc.data_ptr(), vc.data_ptr(), Lc,
+           torch.cuda.current_stream(dev).cuda_stream)
+    torch.cuda.synchronize()
+    assert torch.equal(kc, kc2)
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+@pytest.mark.parametrize("d,pos", [(128, 0), (128, 77), (64, 300)])
+def test_attn_decode_matches_sdpa(dt, d, pos):
+    dev = need_cuda()
+    B, Hq, Hkv, Lc = 2, 8, 2, 512
+    q = torch.randn(B, Hq, d, device=dev).to(dt)
+    kc = torch.randn(B, Hkv, Lc, d, device=dev).to(dt)
+    vc = torch.randn(B, Hkv, Lc, d, device=dev).to(dt)
+    out = torch.empty(B, Hq * d, device=dev, dtype=dt)
+    p = torch.tensor([pos], device=dev)
+    code = L.CBQ_BF16 if dt == torch.bfloat16 else L.CBQ_F32
+    L.call("cbq_attn_decode", q.data_ptr(), kc.data_ptr(), vc.data_ptr(), code, B, Hq, Hkv, d, Lc, p.data_ptr(),
+           d ** -0.5, out.data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
+    kr = kc[:, :, :pos + 1].float().repeat_interleave(Hq // Hkv, dim=1)
+    vr = vc[:, :, :pos + 1].float().repeat_interleave(Hq // Hkv, dim=1)
+    att = torch.softmax((q.float().unsqueeze(2) @ kr.transpose(-1, -2)) * d ** -0.5, dim=-1)
+    ref = (att @ vr).reshape(B, Hq * d)
+    tol = 1e-5 if dt == torch.float32 else 8e-3
+    assert rel_l2(out.float().cpu().numpy(), ref.cpu().numpy()) < tol

@@ -65,13 +65,14 @@ def hf_greedy(m, prompt, n):
 
 @pytest.mark.parametrize("cfg", [TINY, TINY_TIED], ids=lambda c: c.name)
 @pytest.mark.parametrize("huffman", [False, True])
-def test_greedy_tokens_match_hf(cfg, huffman):
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "torch-ops"])
+def test_greedy_tokens_match_hf(cfg, huffman, fused):
     dev = need_cuda()
     W = q3.CompressedQwen3Weights(cfg, dev, huffman=huffman, keep_indices=True, seed=5)
     m = hf_from(W)
     prompt = torch.randint(0, cfg.vocab, (2, 16), generator=torch.Generator().manual_seed(7))
     ref, gap = hf_greedy(m, prompt, 30)
-    dec = qd.Qwen3Decoder(W, batch=2, max_len=64, act_dtype=torch.float32)
+    dec = qd.Qwen3Decoder(W, batch=2, max_len=64, act_dtype=torch.float32, fused=fused)
     eager = dec.generate(prompt, 30).cpu()
     dec.reset()
     dec.capture()
@@ -82,17 +83,38 @@ def test_greedy_tokens_match_hf(cfg, huffman):
     assert torch.equal(graphed, ref), f"greedy tokens differ (smallest top-2 gap {gap:.3e})"
 
 
-def test_bf16_decode_runs_and_mostly_agrees():
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "torch-ops"])
+def test_bf16_decode_runs_and_mostly_agrees(fused):
     """bf16 activations (the bench's setting) against HF in bf16 on the CPU."""
     dev = need_cuda()
     W = q3.CompressedQwen3Weights(TINY, dev, keep_indices=True, seed=9)
     m = hf_from(W).to(torch.bfloat16)
     prompt = torch.randint(0, TINY.vocab, (1, 16), generator=torch.Generator().manual_seed(3))
     ref, _ = hf_greedy(m, prompt, 30)
-    dec = qd.Qwen3Decoder(W, batch=1, max_len=64, act_dtype=torch.bfloat16)
+    dec = qd.Qwen3Decoder(W, batch=1, max_len=64, act_dtype=torch.bfloat16, fused=fused)
     dec.capture()
     dec.reset()
     got = dec.generate(prompt, 30).cpu()
     dec.release()
     agree = int((got == ref).cumprod(1).sum())
     assert agree >= 8, f"bf16 decode agrees with HF bf16 for only {agree} leading tokens"
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+def test_fused_and_torch_op_steps_agree(dt):
+    """The fused step (8 launches per layer) against the torch-op step on the
+    same weights: the element-wise parts round identically, only reduction
+    orders differ, so the logits agree closely and the tokens exactly."""
+    dev = need_cuda()
+    W = q3.CompressedQwen3Weights(TINY_TIED, dev, seed=11)
+    prompt = torch.randint(0, TINY_TIED.vocab, (2, 12), generator=torch.Generator().manual_seed(4))
+    outs, logits = [], []
+    for fused in (True, False):
+        dec = qd.Qwen3Decoder(W, batch=2, max_len=40, act_dtype=dt, fused=fused)
+        outs.append(dec.generate(prompt, 10).cpu())
+        logits.append(dec.logits.float().cpu())
+    tol = 1e-5 if dt == torch.float32 else 2e-2
+    rel = float((logits[0] - logits[1]).norm() / logits[1].norm())
+    assert rel < tol, rel
+    if dt == torch.float32:
+        assert torch.equal(outs[0], outs[1])
