@@ -55,6 +55,7 @@ def parse():
                     help="decode: Qwen3 greedy decode (headline); gemv: one matrix shape, GB/s")
     ap.add_argument("--shape", default="12288,4096", help="gemv workload: M,K")
     ap.add_argument("--tokens", type=int, default=1, help="gemv workload: T (activation rows)")
+    ap.add_argument("--x-dtype", default="bf16", choices=["bf16", "f32"], help="gemv workload: activation dtype")
     return ap.parse_args()
 
 
@@ -232,11 +233,12 @@ def gemv_workload(args):
         else:
             lin = cbq.GPUAcceleratedLinear("g", d["indices"], d["codebook"], (M, K), d["bits"], device=dev)
             b = (M * K * d["bits"] + 7) // 8
-        alg += b + 4 * lin.C + 2 * K * T + 2 * M * T
+        alg += b + 4 * lin.C + (2 if args.x_dtype == "bf16" else 4) * (K + M) * T
         mats.append(lin)
         del bits, d
-    x = torch.randn(T, K, device=dev).to(torch.bfloat16)
-    outs = [torch.empty(T, M, device=dev, dtype=torch.bfloat16) for _ in mats]
+    xdt = torch.bfloat16 if args.x_dtype == "bf16" else torch.float32
+    x = torch.randn(T, K, device=dev).to(xdt)
+    outs = [torch.empty(T, M, device=dev, dtype=xdt) for _ in mats]
     for _ in range(args.warmup):
         for m, o in zip(mats, outs):
             m(x, out=o)
@@ -249,7 +251,7 @@ def gemv_workload(args):
     kern = "k_linear_huff" if args.huffman else "k_linear_fixed"
     line = {"metric": "compressed GEMV GB/s vs HBM", "value": gbs, "unit": "GB/s", "n_gpus": 1,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "scaling": "weak", "vs_baseline": None, "dtype": args.x_dtype,
             "data": "synthetic seeded bf16 N(0,0.02), lossless per-matrix codebook",
             "config": {"workload": f"{kern} {M}x{K} T={T} {'huffman' if args.huffman else 'fixed'}",
                        "copies": R, "l2": f"{R} distinct matrices rotated (> 2x L2)",

@@ -1,4 +1,5 @@
 // cbq_api.cu -- library-wide C ABI entry points and host helpers.
+#include <cstdlib>
 #include <mutex>
 
 #include "cbq_common.cuh"
@@ -31,6 +32,14 @@ const DevInfo &info() {
 
 int sm_count() { return info().sms; }
 int max_smem_optin() { return info().smem_optin; }
+
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char *v = std::getenv("CBQ_PDL");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
 
 }  // namespace cbq_host
 

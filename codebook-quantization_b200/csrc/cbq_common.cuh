@@ -2,6 +2,7 @@
 // (sm_100a): mbarrier + 1-D bulk-copy (TMA) staging, bounded waits, dtype I/O.
 #pragma once
 #include <cuda_runtime.h>
+#include <utility>
 #include <cuda_bf16.h>
 #include <stdint.h>
 
@@ -116,6 +117,19 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
+// Programmatic dependent launch.  A kernel launched with
+// cbq_host::launch_pdl may start while the previous kernel on its stream is
+// still running: it lets its own successor launch as soon as all of its CTAs
+// are running (pdl_launch_dependents, so no launch ever waits for CTAs that
+// cannot be scheduled), does the work that reads nothing the predecessor
+// writes (weight prefetch, tables), then waits for the predecessor to finish
+// and its writes to be visible (pdl_wait) before touching activations.
+// Both are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 }  // namespace cbq
 
 // Host-side helpers shared by the .cu files.
@@ -123,6 +137,25 @@ namespace cbq_host {
 int sm_count();           // SMs of the current device (cached per device)
 int max_smem_optin();     // opt-in dynamic shared memory per block
 inline int64_t align_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
+bool pdl_enabled();       // programmatic dependent launch (CBQ_PDL=0 in the environment turns it off)
+
+// Launch `kern` on `s` with the programmatic-stream-serialization attribute
+// (see pdl_wait above); plain stream order when PDL is off.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 }  // namespace cbq_host
 
 #define CBQ_CUDA_TRY(expr)                                   \

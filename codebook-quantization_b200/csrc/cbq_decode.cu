@@ -41,6 +41,8 @@ template <typename T, int NT>
 __global__ void __launch_bounds__(NT) k_rmsnorm(T *x, const T *add, int64_t n, const float *w, float eps,
                                                 T *out) {
     __shared__ float red[32];
+    pdl_launch_dependents();
+    pdl_wait();
     const int64_t r = blockIdx.x;
     T *xr = x + r * n;
     const T *ar = add ? add + r * n : nullptr;
@@ -74,6 +76,8 @@ __global__ void __launch_bounds__(256) k_qk_norm_rope(const T *q, const T *k, co
                                                       const int64_t *pos_dev, T *q_out, T *k_cache,
                                                       T *v_cache, int64_t L) {
     constexpr int D = 32 * E;
+    pdl_launch_dependents();
+    pdl_wait();
     const int gw = (int)((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5);
     const int lane = threadIdx.x & 31;
     const int per_row = Hq + 2 * Hkv;
@@ -132,6 +136,8 @@ __global__ void __launch_bounds__(D) k_attn_decode(const T *q, const T *k_cache,
     constexpr int NW = D / 32, E = D / 32;
     extern __shared__ float sc[];                 // scores [L]
     __shared__ float red[32];
+    pdl_launch_dependents();
+    pdl_wait();
     const int bh = blockIdx.x;
     const int b = bh / Hq, h = bh - b * Hq;
     const int g = h / (Hq / Hkv);
@@ -192,14 +198,14 @@ extern "C" int cbq_rmsnorm(void *x_dev, const void *add_dev, int dtype, int64_t 
     if (!x_dev || !out_dev || rows > 0x7fffffff) return CBQ_ERR_ARG;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (dtype == CBQ_F32)
-        k_rmsnorm<float, 256><<<(unsigned)rows, 256, 0, s>>>(static_cast<float *>(x_dev),
-                                                             static_cast<const float *>(add_dev), n,
-                                                             weight_dev, eps, static_cast<float *>(out_dev));
+        CBQ_CUDA_TRY(cbq_host::launch_pdl(k_rmsnorm<float, 256>, dim3((unsigned)rows), dim3(256), 0, s,
+                                          static_cast<float *>(x_dev), static_cast<const float *>(add_dev), n,
+                                          weight_dev, eps, static_cast<float *>(out_dev)));
     else
-        k_rmsnorm<__nv_bfloat16, 256><<<(unsigned)rows, 256, 0, s>>>(
-            static_cast<__nv_bfloat16 *>(x_dev), static_cast<const __nv_bfloat16 *>(add_dev), n, weight_dev,
-            eps, static_cast<__nv_bfloat16 *>(out_dev));
-    CBQ_CUDA_TRY(cudaGetLastError());
+        CBQ_CUDA_TRY(cbq_host::launch_pdl(k_rmsnorm<__nv_bfloat16, 256>, dim3((unsigned)rows), dim3(256), 0, s,
+                                          static_cast<__nv_bfloat16 *>(x_dev),
+                                          static_cast<const __nv_bfloat16 *>(add_dev), n, weight_dev, eps,
+                                          static_cast<__nv_bfloat16 *>(out_dev)));
     return CBQ_OK;
 }
 
@@ -219,11 +225,11 @@ extern "C" int cbq_qk_norm_rope(const void *q_dev, const void *k_dev, const void
     const unsigned grid = (unsigned)((warps * 32 + 255) / 256);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
 #define CBQ_QK(T, E)                                                                               \
-    k_qk_norm_rope<T, E><<<grid, 256, 0, s>>>(                                                     \
-        static_cast<const T *>(q_dev), static_cast<const T *>(k_dev), static_cast<const T *>(v_dev), \
-        (int)B, (int)Hq, (int)Hkv, eps, q_weight_dev, k_weight_dev, cos_dev, sin_dev, pos_dev,      \
-        static_cast<T *>(q_out_dev), static_cast<T *>(k_cache_dev), static_cast<T *>(v_cache_dev),  \
-        cache_len)
+    CBQ_CUDA_TRY(cbq_host::launch_pdl(                                                             \
+        k_qk_norm_rope<T, E>, dim3(grid), dim3(256), 0, s, static_cast<const T *>(q_dev),           \
+        static_cast<const T *>(k_dev), static_cast<const T *>(v_dev), (int)B, (int)Hq, (int)Hkv, eps, \
+        q_weight_dev, k_weight_dev, cos_dev, sin_dev, pos_dev, static_cast<T *>(q_out_dev),          \
+        static_cast<T *>(k_cache_dev), static_cast<T *>(v_cache_dev), cache_len))
     if (dtype == CBQ_F32) {
         if (head_dim == 64) CBQ_QK(float, 2); else if (head_dim == 128) CBQ_QK(float, 4); else CBQ_QK(float, 8);
     } else {
@@ -252,10 +258,10 @@ extern "C" int cbq_attn_decode(const void *q_dev, const void *k_cache_dev, const
         if (smem > 48 * 1024)                                                                        \
             CBQ_CUDA_TRY(cudaFuncSetAttribute(k_attn_decode<T, D>,                                   \
                                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
-        k_attn_decode<T, D><<<(unsigned)(B * Hq), D, smem, s>>>(                                     \
-            static_cast<const T *>(q_dev), static_cast<const T *>(k_cache_dev),                      \
-            static_cast<const T *>(v_cache_dev), pos_dev, (int)Hq, (int)Hkv, cache_len, scale,       \
-            static_cast<T *>(out_dev));                                                              \
+        CBQ_CUDA_TRY(cbq_host::launch_pdl(k_attn_decode<T, D>, dim3((unsigned)(B * Hq)), dim3(D), smem, s, \
+                                          static_cast<const T *>(q_dev), static_cast<const T *>(k_cache_dev), \
+                                          static_cast<const T *>(v_cache_dev), pos_dev, (int)Hq, (int)Hkv, \
+                                          cache_len, scale, static_cast<T *>(out_dev)));             \
     } while (0)
     if (dtype == CBQ_F32) {
         if (head_dim == 64) CBQ_AT(float, 64); else if (head_dim == 128) CBQ_AT(float, 128); else CBQ_AT(float, 256);

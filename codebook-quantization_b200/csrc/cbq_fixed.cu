@@ -19,7 +19,7 @@ namespace cbq {
 template <int BITS>
 int launch_fixed_bits(int TB, bool x_bf16, const FixedArgs &a, size_t smem, int grid, cudaStream_t s);
 template <int BITS>
-int launch_gemv_bits(int TB, bool x_bf16, const GemvArgs &a, size_t smem, int grid, cudaStream_t s);
+int launch_gemv_bits(int TB, int NF, bool x_bf16, const GemvArgs &a, size_t smem, int grid, cudaStream_t s);
 }
 
 namespace {
@@ -135,7 +135,7 @@ int64_t workspace_bytes_for(int64_t M, int64_t K, int64_t T) {
 
 // Plan of the one/two-token kernel (k_gemv_fixed); false -> k_linear_fixed.
 struct GemvPlan {
-    int grid = 0, rows_per_cta = 0, nseg = 0;
+    int grid = 0, rows_per_cta = 0, nseg = 0, nf = 32;
     uint32_t H = 0, NP = 0;
     size_t smem = 0;
 };
@@ -146,26 +146,30 @@ bool plan_gemv(int64_t M, int64_t K, int bits, int64_t C, int64_t T, GemvPlan &p
     const int64_t sms = cbq_host::sm_count();
     int64_t rows = (M + sms - 1) / sms;
     if (even_rows) rows += rows & 1;
-    const int nseg = (int)((K + kGvSeg - 1) / kGvSeg);
+    // units of 64 indices per lane when every warp still gets several of them
+    const int64_t units64 = rows * ((K + GvCfg<64>::kSeg - 1) / GvCfg<64>::kSeg);
+    const int nf = (T == 1 && units64 >= 6 * kGvWarps) ? 64 : 32;
+    const int nseg = (int)((K + 32 * nf - 1) / (32 * nf));
     const int64_t NP = (bits <= 14) ? std::max<int64_t>(C, 1ll << bits) : C;
     const size_t budget = (size_t)cbq_host::max_smem_optin();
-    const size_t fixed = kGvBarBytes + gemv_part_bytes((int)rows, nseg, (int)T) + gemv_ring_bytes(bits);
+    const size_t fixed = kGvBarBytes + gemv_part_bytes((int)rows, nseg, (int)T) + gemv_ring_bytes(bits, nf);
     if (fixed + a128((size_t)NP * 4) > budget) return false;
     int64_t H = (int64_t)((budget - fixed - 128 - (size_t)NP * 4) / 124);
     H = std::min<int64_t>(H, C);
     p.grid = (int)((M + rows - 1) / rows);
     p.rows_per_cta = (int)rows;
     p.nseg = nseg;
+    p.nf = nf;
     p.H = (uint32_t)H;
     p.NP = (uint32_t)NP;
     p.smem = fixed + gemv_cb_bytes(p.H, p.NP);
     return p.smem <= budget;
 }
 
-int launch_gemv(int bits, int TB, bool xbf16, const GemvArgs &a, size_t smem, int grid,
+int launch_gemv(int bits, int TB, int NF, bool xbf16, const GemvArgs &a, size_t smem, int grid,
                 cudaStream_t s) {
     switch (bits) {
-#define CBQ_B(n) case n: return launch_gemv_bits<n>(TB, xbf16, a, smem, grid, s);
+#define CBQ_B(n) case n: return launch_gemv_bits<n>(TB, NF, xbf16, a, smem, grid, s);
         CBQ_B(1) CBQ_B(2) CBQ_B(3) CBQ_B(4) CBQ_B(5) CBQ_B(6) CBQ_B(7) CBQ_B(8)
         CBQ_B(9) CBQ_B(10) CBQ_B(11) CBQ_B(12) CBQ_B(13) CBQ_B(14) CBQ_B(15) CBQ_B(16)
 #undef CBQ_B
@@ -201,7 +205,7 @@ int linear_fixed_impl(const void *x, int x_dtype, int64_t T, int64_t ldx, const 
         a.mat[0] = GemvMat{packed, out, bias, nullptr, ldo, (int)M};
         a.out_bf16 = out_dtype == CBQ_BF16;
         a.H = g.H; a.NP = g.NP; a.m128 = 128u; a.m4 = 4u; a.status = nullptr;
-        return launch_gemv(bits, (int)T, x_dtype == CBQ_BF16, a, g.smem, g.grid, s);
+        return launch_gemv(bits, (int)T, g.nf, x_dtype == CBQ_BF16, a, g.smem, g.grid, s);
     }
     if (aligned && plan_fixed(M, K, bits, C, T, xbytes, p)) {
         FixedArgs a{};
@@ -308,7 +312,7 @@ extern "C" int cbq_linear_fixed_multi(const void *x_dev, int x_dtype, int64_t T,
                            resid_dev ? resid_dev[m] : nullptr, ldo[m], (int)M[m]};
     a.out_bf16 = out_dtype == CBQ_BF16;
     a.H = g.H; a.NP = g.NP; a.m128 = 128u; a.m4 = 4u; a.status = nullptr;
-    return launch_gemv(bits, (int)T, x_dtype == CBQ_BF16, a, g.smem, g.grid,
+    return launch_gemv(bits, (int)T, g.nf, x_dtype == CBQ_BF16, a, g.smem, g.grid,
                        static_cast<cudaStream_t>(stream));
 }
 

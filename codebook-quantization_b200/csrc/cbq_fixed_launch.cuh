@@ -64,31 +64,36 @@ int ensure_smem(Kern kern, size_t smem, std::mutex &mu, size_t (&configured)[64]
     return CBQ_OK;
 }
 
-template <int BITS, int TB, typename XT>
+template <int BITS, int TB, int NF, typename XT>
 int launch_gemv_one(const GemvArgs &a, size_t smem, int grid, cudaStream_t s) {
-    auto kern = k_gemv_fixed<BITS, TB, XT>;
+    auto kern = k_gemv_fixed<BITS, TB, NF, XT>;
     static std::mutex mu;
     static size_t configured[64] = {0};
     const int rc = ensure_smem(kern, smem, mu, configured);
     if (rc != CBQ_OK) return rc;
-    kern<<<grid, kGvWarps * 32, smem, s>>>(a);
-    return cudaGetLastError() == cudaSuccess ? CBQ_OK : CBQ_ERR_CUDA;
+    return cbq_host::launch_pdl(kern, dim3(grid), dim3(kGvWarps * 32), smem, s, a) == cudaSuccess
+               ? CBQ_OK
+               : CBQ_ERR_CUDA;
 }
 
+// Token counts 1 and 2 with units of 32 indices per lane, and one token with
+// units of 64.
 template <int BITS>
-int launch_gemv_bits(int TB, bool x_bf16, const GemvArgs &a, size_t smem, int grid, cudaStream_t s) {
+int launch_gemv_bits(int TB, int NF, bool x_bf16, const GemvArgs &a, size_t smem, int grid, cudaStream_t s) {
     if (x_bf16) {
-        if (TB == 1) return launch_gemv_one<BITS, 1, __nv_bfloat16>(a, smem, grid, s);
-        if (TB == 2) return launch_gemv_one<BITS, 2, __nv_bfloat16>(a, smem, grid, s);
+        if (TB == 1 && NF == 64) return launch_gemv_one<BITS, 1, 64, __nv_bfloat16>(a, smem, grid, s);
+        if (TB == 1 && NF == 32) return launch_gemv_one<BITS, 1, 32, __nv_bfloat16>(a, smem, grid, s);
+        if (TB == 2 && NF == 32) return launch_gemv_one<BITS, 2, 32, __nv_bfloat16>(a, smem, grid, s);
     } else {
-        if (TB == 1) return launch_gemv_one<BITS, 1, float>(a, smem, grid, s);
-        if (TB == 2) return launch_gemv_one<BITS, 2, float>(a, smem, grid, s);
+        if (TB == 1 && NF == 64) return launch_gemv_one<BITS, 1, 64, float>(a, smem, grid, s);
+        if (TB == 1 && NF == 32) return launch_gemv_one<BITS, 1, 32, float>(a, smem, grid, s);
+        if (TB == 2 && NF == 32) return launch_gemv_one<BITS, 2, 32, float>(a, smem, grid, s);
     }
     return CBQ_ERR_UNSUPPORTED;
 }
 
 #define CBQ_INSTANTIATE_FIXED(B)                                                              \
     template int launch_fixed_bits<B>(int, bool, const FixedArgs &, size_t, int, cudaStream_t); \
-    template int launch_gemv_bits<B>(int, bool, const GemvArgs &, size_t, int, cudaStream_t);
+    template int launch_gemv_bits<B>(int, int, bool, const GemvArgs &, size_t, int, cudaStream_t);
 
 }  // namespace cbq

@@ -27,7 +27,8 @@
 //     slots (one cp.async.bulk per unit, completing on the slot's mbarrier)
 //     and decodes two rows of a segment at once where it can; the first
 //     copies are issued before the codebook is built so that the DRAM latency
-//     overlaps the table fill.
+//     overlaps the table fill, and with programmatic dependent launch both
+//     happen while the previous kernel on the stream is still finishing.
 #pragma once
 #include "cbq_common.cuh"
 
@@ -36,17 +37,21 @@ namespace cbq {
 #ifndef CBQ_GV_WARPS
 #define CBQ_GV_WARPS 16
 #endif
-#ifndef CBQ_GV_SLOTS
-#define CBQ_GV_SLOTS 3
-#endif
 #ifndef CBQ_GV_PAIR
 #define CBQ_GV_PAIR 1
 #endif
 constexpr int kGvWarps = CBQ_GV_WARPS;   // warps per CTA
-constexpr int kGvSeg = 1024;             // indices per unit (32 lanes x 32)
-constexpr int kGvSlots = CBQ_GV_SLOTS;   // ring slots per warp
-constexpr size_t kGvBarBytes = a128((size_t)kGvWarps * kGvSlots * 8);   // one mbarrier per slot
-static_assert(kGvWarps * 32 <= 1024 && kGvSlots >= 2, "gemv launch shape");
+// A unit is NF indices per lane (32 * NF per warp) of one row: NF = 32 with
+// three ring slots per warp, or NF = 64 with two (fewer per-unit costs for
+// long rows of work, same bytes in flight).
+template <int NF> struct GvCfg {
+    static_assert(NF == 32 || NF == 64, "units of 32 or 64 indices per lane");
+    static constexpr int kSeg = 32 * NF;
+    static constexpr int kSlots = NF == 32 ? 3 : 2;
+};
+constexpr int kGvMaxSlots = 3;
+constexpr size_t kGvBarBytes = a128((size_t)kGvWarps * kGvMaxSlots * 8);   // one mbarrier per slot
+static_assert(kGvWarps * 32 <= 1024, "gemv launch shape");
 
 constexpr int kGvMaxMats = 3;
 
@@ -108,35 +113,37 @@ __host__ __device__ inline size_t gemv_part_bytes(int rows_per_cta, int nseg, in
 __host__ __device__ inline size_t gemv_cb_bytes(uint32_t H, uint32_t NP) {
     return a128((size_t)H * 128 + (size_t)(NP - H) * 4);
 }
-__host__ __device__ inline size_t gemv_ring_bytes(int bits) {
-    return (size_t)kGvWarps * kGvSlots * kGvSeg * bits / 8;
+__host__ __device__ inline size_t gemv_ring_bytes(int bits, int nf) {
+    return (size_t)kGvWarps * (nf == 32 ? GvCfg<32>::kSlots : GvCfg<64>::kSlots) * 32 * nf * bits / 8;
 }
 
-template <int BITS>
-__device__ __forceinline__ void gv_load_share(const uint32_t *p, uint32_t (&w)[BITS + 1]) {
-    // lane stride BITS words: 32-bit loads for odd BITS (conflict-free), wider
-    // loads for even BITS so the lanes' loads stay on distinct banks
-    if constexpr (BITS % 4 == 0) {
+// One lane's share of a unit is NF * BITS / 32 words.
+template <int BITS, int NF>
+__device__ __forceinline__ void gv_load_share(const uint32_t *p, uint32_t (&w)[NF * BITS / 32 + 1]) {
+    // lane stride NW words: 32-bit loads for odd NW (conflict-free), wider
+    // loads for even NW so the lanes' loads stay on distinct banks
+    constexpr int NW = NF * BITS / 32;
+    if constexpr (NW % 4 == 0) {
 #pragma unroll
-        for (int s = 0; s < BITS / 4; ++s) {
+        for (int s = 0; s < NW / 4; ++s) {
             const uint4 v = reinterpret_cast<const uint4 *>(p)[s];
             w[4 * s] = v.x; w[4 * s + 1] = v.y; w[4 * s + 2] = v.z; w[4 * s + 3] = v.w;
         }
-    } else if constexpr (BITS % 2 == 0) {
+    } else if constexpr (NW % 2 == 0) {
 #pragma unroll
-        for (int s = 0; s < BITS / 2; ++s) {
+        for (int s = 0; s < NW / 2; ++s) {
             const uint2 v = reinterpret_cast<const uint2 *>(p)[s];
             w[2 * s] = v.x; w[2 * s + 1] = v.y;
         }
     } else {
 #pragma unroll
-        for (int s = 0; s < BITS; ++s) w[s] = p[s];
+        for (int s = 0; s < NW; ++s) w[s] = p[s];
     }
-    w[BITS] = 0u;
+    w[NW] = 0u;
 }
 
-template <int BITS>
-__device__ __forceinline__ uint32_t gv_field(const uint32_t (&w)[BITS + 1], int i) {
+template <int BITS, int NF>
+__device__ __forceinline__ uint32_t gv_field(const uint32_t (&w)[NF * BITS / 32 + 1], int i) {
     const int bit = i * BITS, wi = bit >> 5, sh = bit & 31;
     constexpr uint32_t mask = (1u << BITS) - 1u;
     const uint32_t v = (sh + BITS <= 32) ? (w[wi] >> sh) : __funnelshift_r(w[wi], w[wi + 1], sh);
@@ -149,25 +156,28 @@ __device__ __forceinline__ float gv_lds(uint32_t addr) {
     return v;
 }
 
-// The 32 activations of lane `lane` in segment s, token row xr (zero past K).
-__device__ __forceinline__ void gv_load_x(const float *xr, int k0, int K, float (&v)[32]) {
+// The NF activations of one lane's share starting at k0, token row xr
+// (zero past K; K is a multiple of 128, so a share is all in or all out).
+template <int NF>
+__device__ __forceinline__ void gv_load_x(const float *xr, int k0, int K, float (&v)[NF]) {
     if (k0 < K) {
         const float4 *p = reinterpret_cast<const float4 *>(xr + k0);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
+        for (int q = 0; q < NF / 4; ++q) {
             const float4 f = __ldg(p + q);
             v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
         }
     } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+        for (int i = 0; i < NF; ++i) v[i] = 0.f;
     }
 }
-__device__ __forceinline__ void gv_load_x(const __nv_bfloat16 *xr, int k0, int K, float (&v)[32]) {
+template <int NF>
+__device__ __forceinline__ void gv_load_x(const __nv_bfloat16 *xr, int k0, int K, float (&v)[NF]) {
     if (k0 < K) {
         const uint4 *p = reinterpret_cast<const uint4 *>(xr + k0);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < NF / 8; ++q) {
             const uint4 f = __ldg(p + q);
             const uint32_t u[4] = {f.x, f.y, f.z, f.w};
 #pragma unroll
@@ -178,17 +188,19 @@ __device__ __forceinline__ void gv_load_x(const __nv_bfloat16 *xr, int k0, int K
         }
     } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+        for (int i = 0; i < NF; ++i) v[i] = 0.f;
     }
 }
 
-template <int BITS, int TB, typename XT>
+template <int BITS, int TB, int NF, typename XT>
 __global__ void __launch_bounds__(kGvWarps * 32, 1) k_gemv_fixed(const GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int kGvSeg = GvCfg<NF>::kSeg, kGvSlots = GvCfg<NF>::kSlots, kNW = NF * BITS / 32;
     constexpr uint32_t kSegBytes = (uint32_t)kGvSeg * BITS / 8;
     constexpr bool kPadded = BITS <= 14;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nseg = a.nseg, K = a.K;
+    pdl_launch_dependents();
     const int64_t m0 = (int64_t)blockIdx.x * a.rows_per_cta;
     if (m0 >= a.M) return;                                   // the whole CTA: no barrier pending
     const int nrows = (int)min((int64_t)a.rows_per_cta, (int64_t)a.M - m0);
@@ -269,6 +281,9 @@ __global__ void __launch_bounds__(kGvWarps * 32, 1) k_gemv_fixed(const GemvArgs 
         }
     }
     __syncthreads();
+    // Weights and codebook are constant; the activations (and the residual
+    // the epilogue reads) come from the previous kernel.
+    pdl_wait();
 
     const uint32_t cb_base = smem_u32(cbs);
     const uint32_t head_off = cb_base + (uint32_t)lane * 4u;
@@ -277,13 +292,13 @@ __global__ void __launch_bounds__(kGvWarps * 32, 1) k_gemv_fixed(const GemvArgs 
     const uint32_t cmax = (uint32_t)(a.C - 1);
     const XT *x = static_cast<const XT *>(a.x);
 
-    float xr[TB][32];
+    float xr[TB][NF];
     int xs = -1;                                             // segment whose x is loaded
     int s = u0 / nrows, rl = u0 - (u0 / nrows) * nrows;      // unit being decoded
     int slot = 0;
     uint32_t phase = 0;
     auto slot_words = [&](int sl) {
-        return reinterpret_cast<const uint32_t *>(ring + (size_t)sl * kSegBytes) + lane * BITS;
+        return reinterpret_cast<const uint32_t *>(ring + (size_t)sl * kSegBytes) + lane * kNW;
     };
     auto gather = [&](uint32_t c) {
         if (!kPadded) c = min(c, cmax);
@@ -292,20 +307,20 @@ __global__ void __launch_bounds__(kGvWarps * 32, 1) k_gemv_fixed(const GemvArgs 
     int i = 0;
     while (i < n) {
         if (s != xs) {
-            const int k0 = s * kGvSeg + lane * 32;
+            const int k0 = s * kGvSeg + lane * NF;
 #pragma unroll
             for (int t = 0; t < TB; ++t) {
-                if (t < a.ntok) gv_load_x(x + (a.t0 + t) * a.ldx, k0, K, xr[t]);
+                if (t < a.ntok) gv_load_x<NF>(x + (a.t0 + t) * a.ldx, k0, K, xr[t]);
                 else {
 #pragma unroll
-                    for (int q = 0; q < 32; ++q) xr[t][q] = 0.f;
+                    for (int q = 0; q < NF; ++q) xr[t][q] = 0.f;
                 }
             }
             xs = s;
         }
         // Two rows of the same segment at once when the range allows: twice
         // the independent gathers in flight per warp.
-        const bool two = CBQ_GV_PAIR && i + 1 < n && rl + 1 < nrows;
+        const bool two = CBQ_GV_PAIR && NF == 32 && i + 1 < n && rl + 1 < nrows;
         const int slot2 = slot + 1 == kGvSlots ? 0 : slot + 1;
         const uint32_t phase2 = slot + 1 == kGvSlots ? phase ^ 1u : phase;
         bool ok = mbar_wait_bounded(&bars[slot], phase);
@@ -317,18 +332,18 @@ __global__ void __launch_bounds__(kGvWarps * 32, 1) k_gemv_fixed(const GemvArgs 
         float acc[2][2][TB];
 #pragma unroll
         for (int t = 0; t < TB; ++t) { acc[0][0][t] = acc[0][1][t] = acc[1][0][t] = acc[1][1][t] = 0.f; }
-        const bool live = s * kGvSeg + lane * 32 < K;
-        uint32_t w[BITS + 1], w2[BITS + 1];
+        const bool live = s * kGvSeg + lane * NF < K;
+        uint32_t w[kNW + 1], w2[kNW + 1];
         if (live) {
-            gv_load_share<BITS>(slot_words(slot), w);
-            if (two) gv_load_share<BITS>(slot_words(slot2), w2);
+            gv_load_share<BITS, NF>(slot_words(slot), w);
+            if (two) gv_load_share<BITS, NF>(slot_words(slot2), w2);
         }
         if (live) {
             if (two) {
 #pragma unroll
-                for (int q = 0; q < 32; ++q) {
-                    const float v = gather(gv_field<BITS>(w, q));
-                    const float v2 = gather(gv_field<BITS>(w2, q));
+                for (int q = 0; q < NF; ++q) {
+                    const float v = gather(gv_field<BITS, NF>(w, q));
+                    const float v2 = gather(gv_field<BITS, NF>(w2, q));
 #pragma unroll
                     for (int t = 0; t < TB; ++t) {
                         acc[0][q & 1][t] = fmaf(xr[t][q], v, acc[0][q & 1][t]);
@@ -337,8 +352,8 @@ __global__ void __launch_bounds__(kGvWarps * 32, 1) k_gemv_fixed(const GemvArgs 
                 }
             } else {
 #pragma unroll
-                for (int q = 0; q < 32; ++q) {
-                    const float v = gather(gv_field<BITS>(w, q));
+                for (int q = 0; q < NF; ++q) {
+                    const float v = gather(gv_field<BITS, NF>(w, q));
 #pragma unroll
                     for (int t = 0; t < TB; ++t) acc[0][q & 1][t] = fmaf(xr[t][q], v, acc[0][q & 1][t]);
                 }
