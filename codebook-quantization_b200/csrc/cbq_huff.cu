@@ -21,6 +21,7 @@
 #include <mutex>
 #include <numeric>
 
+#include "cbq_hgemv_kernel.cuh"
 #include "cbq_huff_kernel.cuh"
 
 namespace {
@@ -157,7 +158,10 @@ __global__ void __launch_bounds__(1024) k_huff_build_lut(const HuffTables *tab, 
         depth[j] = 0;
         if (L0 >= 1 && L0 <= kHfLutBits) {
             lut[p] = (payload(sym) << 16) | (uint32_t)L0;
-        } else if (L0 > kHfLutBits) {
+        } else if (L0 == 0 && code_len_at(tab, (p << (32 - kHfLutBits)) | ((1u << (32 - kHfLutBits)) - 1u),
+                                          sym) == 0) {
+            lut[p] = (payload(0) << 16) | 0x40u | 1u;           // no code starts here: guard
+        } else if (L0 > kHfLutBits || L0 == 0) {
             uint32_t s2;
             int L1 = code_len_at(tab, (p << (32 - kHfLutBits)) | ((1u << (32 - kHfLutBits)) - 1u), s2);
             if (L1 == 0) L1 = 32;                           // incomplete code: cover every bit
@@ -190,25 +194,33 @@ __global__ void __launch_bounds__(1024) k_huff_build_lut(const HuffTables *tab, 
     uint32_t off = warp_tot[warp] + incl - mine;
     uint32_t *sub = lut + kHfLutSize + 4;
     uint32_t used_max = 0;
+    int dropped = 0;
     for (int j = 0; j < kPer; ++j) {
         if (!depth[j]) continue;
         const uint32_t p = (uint32_t)(p0 + j);
         const uint32_t d = depth[j], n = 1u << d;
         if (off + n <= (uint32_t)kHfSubMax) {
-            lut[p] = (off << 16) | (d << 8) | 0x80u;
+            lut[p] = (off << 16) | 0x80u | (32u - d);
             for (uint32_t k = 0; k < n; ++k) {
                 const uint32_t w = (p << (32 - kHfLutBits)) | (k << (32 - kHfLutBits - d));
                 uint32_t sym;
                 const int L = code_len_at(tab, w, sym);
-                sub[off + k] = (L > kHfLutBits) ? ((payload(sym) << 16) | (uint32_t)L) : 0u;
+                sub[off + k] = (L > kHfLutBits) ? ((payload(sym) << 16) | (uint32_t)L)
+                                                : ((payload(0) << 16) | 0x40u | 1u);
             }
             used_max = max(used_max, off + n);
+        } else {
+            dropped = 1;
         }
         off += n;
     }
     used_max = __reduce_max_sync(0xffffffffu, used_max);
     if (lane == 0) atomicMax(&lut[kHfLutSize + 1], used_max);
-    if (threadIdx.x == 0) lut[kHfLutSize] = exact ? 1u : 0u;
+    dropped = __syncthreads_or(dropped);
+    if (threadIdx.x == 0) {
+        lut[kHfLutSize] = exact ? 1u : 0u;
+        lut[kHfLutSize + 2] = dropped ? 0u : 1u;
+    }
 }
 
 // ---------------------------------------------------------------- decode / embedding
@@ -316,6 +328,54 @@ bool plan_huff(int64_t M, int64_t K, int64_t T, int64_t total_bits, int xbytes, 
     p.smem = huff_prefix_bytes((int)K, TB, xbytes) + ring;
     p.grid = cbq_host::sm_count();
     return true;
+}
+
+// One-token kernel (k_gemv_huff): rows per CTA and the ring slot size.
+struct HgPlan {
+    int grid = 0, rows_per_cta = 0, nseg = 0;
+    uint32_t cap = 0;
+    size_t smem = 0;
+};
+
+bool plan_hgemv(int64_t M, int64_t K, int64_t total_bits, HgPlan &p) {
+    if (M <= 0 || K <= 0 || M >= (1ll << 31) || K > (1 << 20)) return false;
+    const int64_t sms = cbq_host::sm_count();
+    const int64_t rows = (M + sms - 1) / sms;
+    const int64_t nch = (K + S - 1) / S;
+    const int nseg = (int)((nch + 31) / 32);
+    const size_t budget = (size_t)cbq_host::max_smem_optin();
+    const size_t prefix = hg_prefix_bytes((int)rows, nseg);
+    if (prefix >= budget) return false;
+    // room for a unit of 1.25x the average code length, capped by shared memory
+    const double avg = std::max(1.0, (double)total_bits / ((double)M * (double)K));
+    const int64_t want = cbq_host::align_up((int64_t)(std::min<int64_t>(K, kHgSeg) * avg / 8.0 * 1.25) + 96, 128);
+    const int64_t room = (int64_t)((budget - prefix) / (kHgWarps * kHgSlots)) & ~(int64_t)127;
+    const int64_t cap = std::min<int64_t>(std::max<int64_t>(want, 1024), room);
+    if (cap < 1024) return false;
+    p.grid = (int)((M + rows - 1) / rows);
+    p.rows_per_cta = (int)rows;
+    p.nseg = nseg;
+    p.cap = (uint32_t)cap;
+    p.smem = prefix + (size_t)kHgWarps * kHgSlots * (size_t)cap;
+    return true;
+}
+
+template <typename XT>
+int launch_hgemv(const HgArgs &a, const HgPlan &p, cudaStream_t s) {
+    auto kern = k_gemv_huff<XT>;
+    static std::mutex mu;
+    static size_t configured[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return CBQ_ERR_CUDA;
+    {
+        std::lock_guard<std::mutex> g(mu);
+        if (configured[dev & 63] < p.smem) {
+            CBQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
+            configured[dev & 63] = p.smem;
+        }
+    }
+    CBQ_CUDA_TRY(cbq_host::launch_pdl(kern, dim3(p.grid), dim3(kHgWarps * 32), p.smem, s, a));
+    return CBQ_OK;
 }
 
 int64_t huff_workspace_bytes(int64_t M, int64_t K, int64_t T) {
@@ -484,6 +544,18 @@ extern "C" int cbq_linear_huff(const void *x_dev, int x_dtype, int64_t T, int64_
     if ((reinterpret_cast<uintptr_t>(stream_dev) & 15) || (reinterpret_cast<uintptr_t>(lut_dev) & 15))
         return CBQ_ERR_ARG;
     if (workspace_dev && workspace_bytes < huff_workspace_bytes(M, K, T)) return CBQ_ERR_ARG;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    HgPlan g;
+    if (T == 1 && (reinterpret_cast<uintptr_t>(x_dev) & 15) == 0 && plan_hgemv(M, K, total_bits, g)) {
+        HgArgs h{};
+        h.x = x_dev; h.ldx = ldx; h.stream = stream_dev; h.stream_bytes = stream_bytes;
+        h.tables = static_cast<const HuffTables *>(tables_dev); h.lut = lut_dev; h.rbs = rbs_dev;
+        h.chunk = chunk_dev; h.total_bits = total_bits; h.codebook = codebook_dev; h.C = (int)C;
+        h.M = (int)M; h.K = (int)K; h.nch = (int)((K + S - 1) / S); h.nseg = g.nseg;
+        h.rows_per_cta = g.rows_per_cta; h.bias = bias_dev; h.out = out_dev; h.ldo = ldo;
+        h.out_bf16 = out_dtype == CBQ_BF16; h.cap = g.cap; h.status = status_dev;
+        return x_dtype == CBQ_BF16 ? launch_hgemv<__nv_bfloat16>(h, g, s) : launch_hgemv<float>(h, g, s);
+    }
     HuffPlan p;
     if (!plan_huff(M, K, T, total_bits, x_dtype == CBQ_BF16 ? 2 : 4, p)) return CBQ_ERR_UNSUPPORTED;
     HuffArgs a{};
@@ -498,7 +570,6 @@ extern "C" int cbq_linear_huff(const void *x_dev, int x_dtype, int64_t T, int64_
         a.part = static_cast<float *>(workspace_dev);
         a.cnt = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(workspace_dev) + pb);
     }
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (x_dtype == CBQ_BF16) return linear_huff_impl<__nv_bfloat16>(a, T, p, s);
     return linear_huff_impl<float>(a, T, p, s);
 }

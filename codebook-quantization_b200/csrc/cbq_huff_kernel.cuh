@@ -57,13 +57,20 @@ __host__ __device__ inline const uint16_t *blob_syms(const HuffTables *t) {
 }
 
 // The decode table (device buffer built by cbq_huff_build_decode_lut):
-//   words [0, 16384): first level.  (payload << 16) | len for len 1..14;
-//     (offset << 16) | (depth << 8) | 0x80 for a prefix of longer codes with
-//     a second-level table; 0 for the canonical search.
+//   words [0, 16384): first level, indexed by the next 14 bits.
+//     (payload << 16) | len for a code of length 1..14;
+//     (payload(0) << 16) | 0x40 | 1 where no code starts with the prefix (an
+//       incomplete code): the reference's guard, symbol 0 consuming one bit;
+//     (offset << 16) | 0x80 | (32 - depth) for a prefix of longer codes: the
+//       code's entry is second-level word offset + (the depth bits after the
+//       prefix), i.e. sub[offset + ((window << 14) >> (32 - depth))];
+//     0 when that prefix's second-level table did not fit (canonical search).
 //   word 16384: mode (1 = payload is the bf16 value, 0 = payload is the
-//     symbol); word 16385: second-level entries used.
+//     symbol); word 16385: second-level entries used; word 16386: 1 when the
+//     two levels decode every 32-bit window (no 0 entries).
 //   words [16388, 16388 + 6144): second level, (payload << 16) | len
-//     (len 15..32; 0 = canonical search).
+//     (len 15..32), or the guard entry above for bit patterns that match no
+//     code.
 struct HuffSlow {                     // shared copy of the canonical tables
     uint64_t limit[kHfMaxLen + 1];
     uint64_t first[kHfMaxLen + 1];
@@ -215,10 +222,7 @@ __device__ __forceinline__ float huff_long(Bits32 &bb, uint32_t e, const uint32_
                                            uint32_t &bad, bool count) {
     if (bb.nb < 32) bb.refill();
     uint32_t e2 = 0;
-    if (e & 0x80u) {
-        const uint32_t d = (e >> 8) & 31u;
-        e2 = sub[(e >> 16) + ((bb.hi << kHfLutBits) >> (32 - d))];
-    }
+    if (e & 0x80u) e2 = sub[(e >> 16) + ((bb.hi << kHfLutBits) >> (e & 0x3fu))];
     float wt;
     int len = (int)(e2 & 0x3fu);
     if (len) {
@@ -252,7 +256,7 @@ __device__ __forceinline__ void huff_chunk(const uint32_t *words, uint32_t nw, u
         for (int q = 0; q < 8; ++q) {
             if ((q & 1) == 0 && bb.nb < 32) bb.refill();   // >= 32 bits for every pair of symbols
             const uint32_t e = lut[bb.hi >> (32 - kHfLutBits)];
-            const int len = (int)(e & 0x3fu);
+            const int len = (e & 0x80u) ? 0 : (int)(e & 0x3fu);
             float wt;
             if (len) {
                 wt = VALUE ? __uint_as_float(e & 0xffff0000u) : __ldg(gcb + min(e >> 16, cmax));
