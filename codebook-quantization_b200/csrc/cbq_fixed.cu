@@ -16,6 +16,9 @@
 #include "cbq_gemv_kernel.cuh"
 
 namespace cbq {
+int gemm_fixed(const void *x, int64_t T, int64_t ldx, const uint8_t *packed, const float *cb, int64_t C,
+               int bits, int64_t M, int64_t K, const float *bias, void *out, int out_dtype, int64_t ldo,
+               cudaStream_t s);
 template <int BITS>
 int launch_fixed_bits(int TB, bool x_bf16, const FixedArgs &a, size_t smem, int grid, cudaStream_t s);
 template <int BITS>
@@ -133,6 +136,9 @@ int64_t workspace_bytes_for(int64_t M, int64_t K, int64_t T) {
     return cbq_host::align_up(M * nseg * TB * 4, 256) + cbq_host::align_up(M * 4, 256);
 }
 
+// Token count from which cbq_linear_fixed uses the tensor-core GEMM.
+constexpr int64_t kGemmMinTokens = 64;
+
 // Plan of the one/two-token kernel (k_gemv_fixed); false -> k_linear_fixed.
 struct GemvPlan {
     int grid = 0, rows_per_cta = 0, nseg = 0, nf = 32;
@@ -196,6 +202,11 @@ int linear_fixed_impl(const void *x, int x_dtype, int64_t T, int64_t ldx, const 
     const bool aligned = (reinterpret_cast<uintptr_t>(packed) & 15) == 0;
     const int xbytes = x_dtype == CBQ_BF16 ? 2 : 4;
     const bool x_aligned = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (ldx * xbytes) % 16 == 0;
+    // many tokens, bf16 activations: the tensor-core GEMM (cbq_gemm.cu)
+    if (T >= kGemmMinTokens && x_dtype == CBQ_BF16) {
+        const int rc = gemm_fixed(x, T, ldx, packed, cb, C, bits, M, K, bias, out, out_dtype, ldo, s);
+        if (rc != CBQ_ERR_UNSUPPORTED) return rc;
+    }
     GemvPlan g;
     if (aligned && x_aligned && plan_gemv(M, K, bits, C, T, g)) {
         GemvArgs a{};

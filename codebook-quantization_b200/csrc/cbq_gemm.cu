@@ -1,0 +1,393 @@
+// cbq_gemm.cu -- fixed-width codebook GEMM for many tokens (prefill) on the
+// 5th-generation tensor cores (sm_100a: tcgen05.mma, TMEM accumulators, TMA).
+//
+// y[t, r] = sum_k x[t, k] * cb[min(idx(r*K + k), C-1)] (+ bias[r]) for a bf16
+// activation matrix x [T, K]; the weights never exist in memory as a matrix:
+// each 128 x 64 weight tile is decoded from the packed LSB-first index stream
+// (reference src/bitpack.py:32-94) straight into shared memory as bf16, in
+// the layout the tensor core reads, once per output tile.
+//
+// One persistent CTA per SM walks output tiles of 128 weight rows x 256
+// tokens.  Warp roles:
+//   * warps 0-3 (128 threads, thread i = tile row i): decode the row's 64
+//     indices of each K step (b 32-bit words from global memory, prefetched
+//     one step ahead), gather bf16 codebook values from shared memory and store
+//     the 128-byte row with the 128-byte swizzle; after the tile's last step
+//     they read the fp32 accumulator out of TMEM (their warp's 32 lanes) and
+//     write y;
+//   * warp 4: TMA loads of the x tile (256 tokens x 64 k, bf16, 128-byte
+//     swizzle, no multicast) into the stage;
+//   * warp 5: owns the TMEM allocation (256 columns = the 128 x 256 fp32
+//     accumulator) and one elected thread issues 4 tcgen05.mma (M=128, N=256,
+//     K=16) per stage, then tcgen05.commit to the stage's "empty" barrier.
+// Four stages of (A 16 KB + B 32 KB) are in flight.  Every mbarrier wait is
+// bounded; on a timeout the CTA records CBQ_FLAG_TIMEOUT, all roles stop at
+// the next wait, and the TMEM is released before the kernel returns.
+#include <cuda.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "cbq_common.cuh"
+
+namespace {
+
+using namespace cbq;
+
+constexpr int kBM = 128, kBN = 256, kBK = 64, kStages = 4;
+constexpr int kDecoders = 128;
+constexpr int kThreads = kDecoders + 64;              // + TMA warp + MMA warp
+constexpr uint32_t kABytes = kBM * kBK * 2;           // 16 KB
+constexpr uint32_t kBBytes = kBN * kBK * 2;           // 32 KB
+constexpr uint32_t kTmemCols = 256;
+
+struct GemmArgs {
+    const uint8_t *packed;
+    const float *codebook;
+    int C, bits;
+    int M, K, T;
+    const float *bias;
+    void *out;
+    int64_t ldo;
+    int out_bf16;
+    int tiles_m, tiles_n;
+    uint32_t cb_entries;              // bf16 codebook entries in shared memory (padded to 2^b)
+    uint32_t *status;
+};
+
+// ---------------------------------------------------------------- PTX helpers
+
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+    // K-major, 128-byte swizzle: rows of 128 bytes, 8-row atoms 1024 bytes apart.
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// kind::f16 instruction descriptor: D fp32, A and B bf16, both K-major, M x N.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int c0, int c1, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_u32(dst)), "l"(map), "r"(c0), "r"(c1), "r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
+    uint16_t v;
+    asm("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
+    return v;
+}
+
+template <int BITS>
+__device__ __forceinline__ uint32_t field64(const uint32_t (&w)[2 * BITS + 1], int i) {
+    const int bit = i * BITS, wi = bit >> 5, sh = bit & 31;
+    constexpr uint32_t mask = (1u << BITS) - 1u;
+    const uint32_t v = (sh + BITS <= 32) ? (w[wi] >> sh) : __funnelshift_r(w[wi], w[wi + 1], sh);
+    return v & mask;
+}
+
+// Bounded wait shared by all roles: false once this CTA has given up.
+__device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
+                                              const GemmArgs &a) {
+    if (*abort_flag) return false;
+    if (mbar_wait_bounded(bar, parity)) return true;
+    *abort_flag = 1;
+    report(a.status, CBQ_FLAG_TIMEOUT, 0u);
+    return false;
+}
+
+template <int BITS>
+__global__ void __launch_bounds__(kThreads, 1) k_gemm_fixed(const __grid_constant__ CUtensorMap tmap_x,
+                                                            const GemmArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // 1024-byte aligned base for the swizzled operand tiles
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t *sA = smem;                                       // kStages x 16 KB
+    uint8_t *sB = sA + kStages * kABytes;                     // kStages x 32 KB
+    uint16_t *scb = reinterpret_cast<uint16_t *>(sB + kStages * kBBytes);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(scb) + a128(a.cb_entries * 2));
+    uint64_t *full_a = bars, *full_b = bars + kStages, *empty = bars + 2 * kStages;
+    uint64_t *acc_full = bars + 3 * kStages, *acc_empty = acc_full + 1, *drain = acc_full + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    pdl_launch_dependents();
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full_a[s], kDecoders);
+            mbar_init(&full_b[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(acc_full, 1);
+        mbar_init(acc_empty, kDecoders);
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        mbar_fence_init();
+    }
+    if (warp == 5) {                                          // TMEM: the 128 x 256 fp32 accumulator
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(smem_u32(tmem_slot)), "r"(kTmemCols) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    // bf16 codebook, padded to cb_entries with cb[C-1] (the reference's clamp)
+    for (uint32_t c = tid; c < a.cb_entries; c += kThreads)
+        scb[c] = __bfloat16_as_ushort(__float2bfloat16_rn(__ldg(a.codebook + min((int)c, a.C - 1))));
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const int nk = a.K / kBK;
+    const int ntiles = a.tiles_m * a.tiles_n;
+
+    if (warp < 4) {
+        // ------------------------------------------------ decoders + epilogue
+        const int r = tid;                                    // tile row
+        const uint32_t cb_s = smem_u32(scb);
+        const int64_t row_words = (int64_t)a.K * BITS / 32;   // 32-bit words per weight row
+        constexpr int NW = 2 * BITS;                          // words per 64-index step
+        int it = 0;                                           // stage uses so far (global step counter)
+        uint32_t acc_phase = 0;
+        bool go = true;
+        pdl_wait();                                           // x and y belong to the stream's previous work
+        for (int tile = blockIdx.x; tile < ntiles && go; tile += gridDim.x) {
+            const int tm = tile / a.tiles_n, tn = tile - tm * a.tiles_n;
+            const int64_t row = (int64_t)tm * kBM + r;
+            const uint32_t *src = reinterpret_cast<const uint32_t *>(a.packed) + row * row_words;
+            uint32_t w[NW + 1], wn[NW + 1];
+#pragma unroll
+            for (int j = 0; j < NW; ++j) wn[j] = __ldg(src + j);
+            for (int k = 0; k < nk; ++k, ++it) {
+#pragma unroll
+                for (int j = 0; j < NW; ++j) w[j] = wn[j];
+                w[NW] = 0u;
+                if (k + 1 < nk) {                             // next step's words, one step ahead
+#pragma unroll
+                    for (int j = 0; j < NW; ++j) wn[j] = __ldg(src + (int64_t)(k + 1) * NW + j);
+                }
+                const int s = it % kStages;
+                if (it >= kStages && !wait_or_abort(&empty[s], ((it / kStages) - 1) & 1, abort_flag, a)) {
+                    go = false;
+                    break;
+                }
+                uint8_t *dst = sA + (size_t)s * kABytes + (size_t)r * 128;
+#pragma unroll
+                for (int ch = 0; ch < 8; ++ch) {              // 8 chunks of 8 bf16 (16 bytes)
+                    uint32_t p[4];
+#pragma unroll
+                    for (int h = 0; h < 4; ++h) {
+                        const uint32_t lo = lds_u16(cb_s + 2u * field64<BITS>(w, ch * 8 + 2 * h));
+                        const uint32_t hi = lds_u16(cb_s + 2u * field64<BITS>(w, ch * 8 + 2 * h + 1));
+                        p[h] = lo | (hi << 16);
+                    }
+                    *reinterpret_cast<uint4 *>(dst + ((ch ^ (r & 7)) << 4)) = make_uint4(p[0], p[1], p[2], p[3]);
+                }
+                fence_proxy_async_smem();                     // generic stores -> tensor-core reads
+                mbar_arrive(&full_a[s]);
+            }
+            if (!go) break;
+            // epilogue: accumulator rows 32*warp.. of this tile
+            if (!wait_or_abort(acc_full, acc_phase, abort_flag, a)) { go = false; break; }
+            acc_phase ^= 1u;
+            tc_fence_after();
+            const int64_t m = (int64_t)tm * kBM + r;
+            const float b = a.bias ? a.bias[m] : 0.f;
+#pragma unroll 1
+            for (int c0 = 0; c0 < kBN; c0 += 32) {
+                uint32_t v[32];
+                tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int64_t t = (int64_t)tn * kBN + c0 + j;
+                    if (t < a.T) {
+                        const float y = __uint_as_float(v[j]) + b;
+                        if (a.out_bf16) static_cast<__nv_bfloat16 *>(a.out)[t * a.ldo + m] = __float2bfloat16_rn(y);
+                        else static_cast<float *>(a.out)[t * a.ldo + m] = y;
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(acc_empty);
+        }
+    } else if (warp == 4) {
+        // ------------------------------------------------------------ TMA (x)
+        if (lane == 0) {
+            int it = 0;
+            bool go = true;
+            pdl_wait();
+            for (int tile = blockIdx.x; tile < ntiles && go; tile += gridDim.x) {
+                const int tn = tile % a.tiles_n;
+                for (int k = 0; k < nk; ++k, ++it) {
+                    const int s = it % kStages;
+                    if (it >= kStages && !wait_or_abort(&empty[s], ((it / kStages) - 1) & 1, abort_flag, a)) {
+                        go = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full_b[s], kBBytes);
+                    tma_load_2d(sB + (size_t)s * kBBytes, &tmap_x, k * kBK, tn * kBN, &full_b[s]);
+                }
+            }
+            // No load may still be landing when the CTA exits: wait (bounded)
+            // for the last load issued into every stage.
+            for (int s = 0; s < kStages && s < it; ++s) {
+                const int last = it - 1 - ((it - 1 - s) % kStages);   // last step that used stage s
+                mbar_wait_bounded(&full_b[s], (last / kStages) & 1);
+            }
+        }
+    } else {
+        // ------------------------------------------------------------- MMA issue
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_bf16(kBM, kBN);
+            int it = 0, nt = 0;
+            bool go = true;
+            for (int tile = blockIdx.x; tile < ntiles && go; tile += gridDim.x, ++nt) {
+                if (nt > 0 && !wait_or_abort(acc_empty, (nt - 1) & 1, abort_flag, a)) { go = false; break; }
+                tc_fence_after();
+                for (int k = 0; k < nk; ++k, ++it) {
+                    const int s = it % kStages;
+                    const uint32_t ph = (it / kStages) & 1;
+                    if (!wait_or_abort(&full_a[s], ph, abort_flag, a) ||
+                        !wait_or_abort(&full_b[s], ph, abort_flag, a)) {
+                        go = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sA + (size_t)s * kABytes), b0 = smem_u32(sB + (size_t)s * kBBytes);
+#pragma unroll
+                    for (int kk = 0; kk < kBK / 16; ++kk)
+                        mma_bf16(tmem, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32), idesc,
+                                 (k > 0 || kk > 0) ? 1u : 0u);
+                    mma_commit(&empty[s]);                    // frees the stage when these MMAs finish
+                }
+                if (!go) break;
+                mma_commit(acc_full);                         // accumulator complete
+            }
+            if (!go || *abort_flag) {                         // gave up: let issued MMAs finish first
+                mma_commit(drain);
+                mbar_wait_bounded(drain, 0);
+            }
+        }
+    }
+    // every role is done (or gave up): release the TMEM
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 5) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    }
+}
+
+// ---------------------------------------------------------------- host side
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return (EncodeTiledFn) nullptr;
+        return reinterpret_cast<EncodeTiledFn>(p);
+    }();
+    return fn;
+}
+
+size_t gemm_smem_bytes(uint32_t cb_entries) {
+    return 1024 + (size_t)kStages * (kABytes + kBBytes) + a128((size_t)cb_entries * 2) + 256;
+}
+
+template <int BITS>
+int launch_gemm(const CUtensorMap &map, const GemmArgs &a, size_t smem, int grid, cudaStream_t s) {
+    auto kern = k_gemm_fixed<BITS>;
+    static std::mutex mu;
+    static size_t configured[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return CBQ_ERR_CUDA;
+    {
+        std::lock_guard<std::mutex> g(mu);
+        if (configured[dev & 63] < smem) {
+            CBQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            configured[dev & 63] = smem;
+        }
+    }
+    CBQ_CUDA_TRY(cbq_host::launch_pdl(kern, dim3(grid), dim3(kThreads), smem, s, map, a));
+    return CBQ_OK;
+}
+
+}  // namespace
+
+namespace cbq {
+
+// Prefill GEMM entry used by cbq_linear_fixed for many tokens.  Returns
+// CBQ_ERR_UNSUPPORTED (nothing launched) outside its shapes: bf16 x with
+// 16-byte aligned rows, M % 128 == 0, K % 64 == 0, b <= 14.
+int gemm_fixed(const void *x, int64_t T, int64_t ldx, const uint8_t *packed, const float *cb, int64_t C,
+               int bits, int64_t M, int64_t K, const float *bias, void *out, int out_dtype, int64_t ldo,
+               cudaStream_t s) {
+    if (bits < 1 || bits > 14 || M % kBM || K % kBK || K <= 0 || T <= 0 || M <= 0) return CBQ_ERR_UNSUPPORTED;
+    if ((reinterpret_cast<uintptr_t>(x) & 15) || (ldx * 2) % 16 || (reinterpret_cast<uintptr_t>(packed) & 3))
+        return CBQ_ERR_UNSUPPORTED;
+    if (M >= (1ll << 31) || T >= (1ll << 31) || K >= (1ll << 31)) return CBQ_ERR_UNSUPPORTED;
+    const uint32_t entries = std::max<uint32_t>((uint32_t)C, 1u << bits);
+    const size_t smem = gemm_smem_bytes(entries);
+    if (smem > (size_t)cbq_host::max_smem_optin()) return CBQ_ERR_UNSUPPORTED;
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return CBQ_ERR_UNSUPPORTED;
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)T};
+    const cuuint64_t strides[1] = {(cuuint64_t)ldx * 2};
+    const cuuint32_t box[2] = {kBK, kBN};
+    const cuuint32_t estr[2] = {1, 1};
+    if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(x), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return CBQ_ERR_UNSUPPORTED;
+    GemmArgs a{};
+    a.packed = packed; a.codebook = cb; a.C = (int)C; a.bits = bits;
+    a.M = (int)M; a.K = (int)K; a.T = (int)T; a.bias = bias; a.out = out; a.ldo = ldo;
+    a.out_bf16 = out_dtype == CBQ_BF16; a.tiles_m = (int)(M / kBM); a.tiles_n = (int)((T + kBN - 1) / kBN);
+    a.cb_entries = entries; a.status = nullptr;
+    const int grid = (int)std::min<int64_t>((int64_t)a.tiles_m * a.tiles_n, cbq_host::sm_count());
+    switch (bits) {
+#define CBQ_G(n) case n: return launch_gemm<n>(map, a, smem, grid, s);
+        CBQ_G(1) CBQ_G(2) CBQ_G(3) CBQ_G(4) CBQ_G(5) CBQ_G(6) CBQ_G(7)
+        CBQ_G(8) CBQ_G(9) CBQ_G(10) CBQ_G(11) CBQ_G(12) CBQ_G(13) CBQ_G(14)
+#undef CBQ_G
+    }
+    return CBQ_ERR_UNSUPPORTED;
+}
+
+}  // namespace cbq
