@@ -9,15 +9,16 @@
 //
 // One persistent CTA per SM walks output tiles of 128 weight rows x 256
 // tokens.  Warp roles:
-//   * warps 0-3 (128 threads, thread i = tile row i): decode the row's 64
-//     indices of each K step (b 32-bit words from global memory, prefetched
-//     one step ahead), gather bf16 codebook values from shared memory and store
-//     the 128-byte row with the 128-byte swizzle; after the tile's last step
-//     they read the fp32 accumulator out of TMEM (their warp's 32 lanes) and
-//     write y;
-//   * warp 4: TMA loads of the x tile (256 tokens x 64 k, bf16, 128-byte
+//   * warps 0-15: two decoder sets of 256 threads (two per tile row) take
+//     alternate K steps; a thread decodes 32 of its row's 64 indices per step
+//     (b 32-bit words from global memory, prefetched two of its steps ahead),
+//     gathers bf16 codebook values from shared memory and stores its four
+//     16-byte chunks of the row with the 128-byte swizzle; after the tile's
+//     last step all 16 warps read the fp32 accumulator out of TMEM (warp w:
+//     lanes 32*(w%4).., a quarter of the columns) and write y;
+//   * warp 16: TMA loads of the x tile (256 tokens x 64 k, bf16, 128-byte
 //     swizzle, no multicast) into the stage;
-//   * warp 5: owns the TMEM allocation (256 columns = the 128 x 256 fp32
+//   * warp 17: owns the TMEM allocation (256 columns = the 128 x 256 fp32
 //     accumulator) and one elected thread issues 4 tcgen05.mma (M=128, N=256,
 //     K=16) per stage, then tcgen05.commit to the stage's "empty" barrier.
 // Four stages of (A 16 KB + B 32 KB) are in flight.  Every mbarrier wait is
@@ -34,8 +35,19 @@ namespace {
 
 using namespace cbq;
 
-constexpr int kBM = 128, kBN = 256, kBK = 64, kStages = 4;
-constexpr int kDecoders = 128;
+constexpr int kBM = 128, kBN = 256, kBK = 64;
+constexpr int kPStages = 2;                           // packed-index tiles (two K steps each) in flight
+// operand stages (A + B): as many as shared memory allows next to the
+// packed tiles and the bf16 codebook
+template <int BITS> struct GemmCfg {
+    static constexpr int kStages = BITS <= 13 ? 3 : 2;
+    static constexpr uint32_t kPRowBytes = 16u * BITS;           // 128 indices of one row
+    static constexpr uint32_t kPBytes = kBM * kPRowBytes;         // one packed tile
+};
+constexpr int kSetThreads = 256;                      // a decoder set: two threads per tile row
+constexpr int kSets = 2;                              // sets decode alternate K steps
+constexpr int kDecoders = kSets * kSetThreads;
+constexpr int kDecWarps = kDecoders / 32;
 constexpr int kThreads = kDecoders + 64;              // + TMA warp + MMA warp
 constexpr uint32_t kABytes = kBM * kBK * 2;           // 16 KB
 constexpr uint32_t kBBytes = kBN * kBK * 2;           // 32 KB
@@ -109,7 +121,7 @@ __device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
 }
 
 template <int BITS>
-__device__ __forceinline__ uint32_t field64(const uint32_t (&w)[2 * BITS + 1], int i) {
+__device__ __forceinline__ uint32_t field32(const uint32_t (&w)[BITS + 1], int i) {
     const int bit = i * BITS, wi = bit >> 5, sh = bit & 31;
     constexpr uint32_t mask = (1u << BITS) - 1u;
     const uint32_t v = (sh + BITS <= 32) ? (w[wi] >> sh) : __funnelshift_r(w[wi], w[wi + 1], sh);
@@ -128,16 +140,21 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, vo
 
 template <int BITS>
 __global__ void __launch_bounds__(kThreads, 1) k_gemm_fixed(const __grid_constant__ CUtensorMap tmap_x,
+                                                            const __grid_constant__ CUtensorMap tmap_p,
                                                             const GemmArgs a) {
+    constexpr int kStages = GemmCfg<BITS>::kStages;
+    constexpr uint32_t kPRowBytes = GemmCfg<BITS>::kPRowBytes, kPBytes = GemmCfg<BITS>::kPBytes;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte aligned base for the swizzled operand tiles
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t *sA = smem;                                       // kStages x 16 KB
     uint8_t *sB = sA + kStages * kABytes;                     // kStages x 32 KB
-    uint16_t *scb = reinterpret_cast<uint16_t *>(sB + kStages * kBBytes);
+    uint8_t *sP = sB + kStages * kBBytes;                     // kPStages packed tiles
+    uint16_t *scb = reinterpret_cast<uint16_t *>(sP + kPStages * a128(kPBytes));
     uint64_t *bars = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(scb) + a128(a.cb_entries * 2));
     uint64_t *full_a = bars, *full_b = bars + kStages, *empty = bars + 2 * kStages;
-    uint64_t *acc_full = bars + 3 * kStages, *acc_empty = acc_full + 1, *drain = acc_full + 2;
+    uint64_t *full_p = bars + 3 * kStages, *empty_p = full_p + kPStages;
+    uint64_t *acc_full = empty_p + kPStages, *acc_empty = acc_full + 1, *drain = acc_full + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
@@ -145,9 +162,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_fixed(const __grid_constan
     pdl_launch_dependents();
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
-            mbar_init(&full_a[s], kDecoders);
+            mbar_init(&full_a[s], kSetThreads);
             mbar_init(&full_b[s], 1);
             mbar_init(&empty[s], 1);
+        }
+        for (int s = 0; s < kPStages; ++s) {
+            mbar_init(&full_p[s], 1);
+            mbar_init(&empty_p[s], kDecoders);               // both decoder sets read a packed tile
         }
         mbar_init(acc_full, 1);
         mbar_init(acc_empty, kDecoders);
@@ -155,7 +176,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_fixed(const __grid_constan
         *abort_flag = 0;
         mbar_fence_init();
     }
-    if (warp == 5) {                                          // TMEM: the 128 x 256 fp32 accumulator
+    if (warp == kDecWarps + 1) {                              // TMEM: the 128 x 256 fp32 accumulator
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                      ::"r"(smem_u32(tmem_slot)), "r"(kTmemCols) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -170,31 +191,41 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_fixed(const __grid_constan
     const int nk = a.K / kBK;
     const int ntiles = a.tiles_m * a.tiles_n;
 
-    if (warp < 4) {
+    if (warp < kDecWarps) {
         // ------------------------------------------------ decoders + epilogue
-        const int r = tid;                                    // tile row
+        // set g = t / 256 decodes the K steps k = g, g + 2, ...; within a set,
+        // thread t: tile row r, half h of the row's 64 indices (BITS words,
+        // 4 chunks of 16 bytes of the swizzled row)
+        const int g = tid / kSetThreads, t = tid % kSetThreads;
+        const int r = t & (kBM - 1), h = t >> 7;
         const uint32_t cb_s = smem_u32(scb);
-        const int64_t row_words = (int64_t)a.K * BITS / 32;   // 32-bit words per weight row
-        constexpr int NW = 2 * BITS;                          // words per 64-index step
-        int it = 0;                                           // stage uses so far (global step counter)
+        constexpr int NW = BITS;                              // words per half step (32 indices)
+        int base_it = 0;                                      // stage uses before this tile
         uint32_t acc_phase = 0;
         bool go = true;
         pdl_wait();                                           // x and y belong to the stream's previous work
-        for (int tile = blockIdx.x; tile < ntiles && go; tile += gridDim.x) {
+        for (int tile = blockIdx.x; tile < ntiles && go; tile += gridDim.x, base_it += nk) {
             const int tm = tile / a.tiles_n, tn = tile - tm * a.tiles_n;
-            const int64_t row = (int64_t)tm * kBM + r;
-            const uint32_t *src = reinterpret_cast<const uint32_t *>(a.packed) + row * row_words;
-            uint32_t w[NW + 1], wn[NW + 1];
-#pragma unroll
-            for (int j = 0; j < NW; ++j) wn[j] = __ldg(src + j);
-            for (int k = 0; k < nk; ++k, ++it) {
-#pragma unroll
-                for (int j = 0; j < NW; ++j) w[j] = wn[j];
-                w[NW] = 0u;
-                if (k + 1 < nk) {                             // next step's words, one step ahead
-#pragma unroll
-                    for (int j = 0; j < NW; ++j) wn[j] = __ldg(src + (int64_t)(k + 1) * NW + j);
+            uint32_t w[NW + 1];
+            for (int k = g; k < nk; k += kSets) {
+                // this row's words of step k from the packed tile (two steps per tile)
+                const int pi = (base_it + k) >> 1;            // packed tiles used before
+                const int ps = pi % kPStages;
+                if (!wait_or_abort(&full_p[ps], (pi / kPStages) & 1, abort_flag, a)) {
+                    go = false;
+                    break;
                 }
+                const uint32_t pw = smem_u32(sP + (size_t)ps * a128(kPBytes)) + (uint32_t)r * kPRowBytes +
+                                    (uint32_t)(k & 1) * (8u * BITS) + (uint32_t)h * (4u * BITS);
+#pragma unroll
+                for (int j = 0; j < NW; ++j) {
+                    uint32_t v;
+                    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(pw + 4u * j));
+                    w[j] = v;
+                }
+                w[NW] = 0u;
+                mbar_arrive(&empty_p[ps]);                    // words are in registers
+                const int it = base_it + k;
                 const int s = it % kStages;
                 if (it >= kStages && !wait_or_abort(&empty[s], ((it / kStages) - 1) & 1, abort_flag, a)) {
                     go = false;
@@ -202,52 +233,67 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_fixed(const __grid_constan
                 }
                 uint8_t *dst = sA + (size_t)s * kABytes + (size_t)r * 128;
 #pragma unroll
-                for (int ch = 0; ch < 8; ++ch) {              // 8 chunks of 8 bf16 (16 bytes)
+                for (int c = 0; c < 4; ++c) {                 // 4 chunks of 8 bf16 (16 bytes)
                     uint32_t p[4];
 #pragma unroll
-                    for (int h = 0; h < 4; ++h) {
-                        const uint32_t lo = lds_u16(cb_s + 2u * field64<BITS>(w, ch * 8 + 2 * h));
-                        const uint32_t hi = lds_u16(cb_s + 2u * field64<BITS>(w, ch * 8 + 2 * h + 1));
-                        p[h] = lo | (hi << 16);
+                    for (int q = 0; q < 4; ++q) {
+                        const uint32_t lo = lds_u16(cb_s + 2u * field32<BITS>(w, c * 8 + 2 * q));
+                        const uint32_t hi = lds_u16(cb_s + 2u * field32<BITS>(w, c * 8 + 2 * q + 1));
+                        p[q] = __byte_perm(lo, hi, 0x5410);
                     }
+                    const int ch = 4 * h + c;
                     *reinterpret_cast<uint4 *>(dst + ((ch ^ (r & 7)) << 4)) = make_uint4(p[0], p[1], p[2], p[3]);
                 }
                 fence_proxy_async_smem();                     // generic stores -> tensor-core reads
                 mbar_arrive(&full_a[s]);
             }
             if (!go) break;
-            // epilogue: accumulator rows 32*warp.. of this tile
+            // epilogue: TMEM lanes 32*(warp%4).. = tile rows; the four warps of
+            // a lane quarter take 64 accumulator columns each
             if (!wait_or_abort(acc_full, acc_phase, abort_flag, a)) { go = false; break; }
             acc_phase ^= 1u;
             tc_fence_after();
-            const int64_t m = (int64_t)tm * kBM + r;
+            const int er = (warp & 3) * 32 + lane;
+            const int64_t m = (int64_t)tm * kBM + er;
             const float b = a.bias ? a.bias[m] : 0.f;
+            const int cbeg = (warp >> 2) * (kBN / 4);
 #pragma unroll 1
-            for (int c0 = 0; c0 < kBN; c0 += 32) {
+            for (int c0 = cbeg; c0 < cbeg + kBN / 4; c0 += 32) {
                 uint32_t v[32];
-                tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+                tmem_ld32(tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)c0, v);
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
-                    const int64_t t = (int64_t)tn * kBN + c0 + j;
-                    if (t < a.T) {
+                    const int64_t tt = (int64_t)tn * kBN + c0 + j;
+                    if (tt < a.T) {
                         const float y = __uint_as_float(v[j]) + b;
-                        if (a.out_bf16) static_cast<__nv_bfloat16 *>(a.out)[t * a.ldo + m] = __float2bfloat16_rn(y);
-                        else static_cast<float *>(a.out)[t * a.ldo + m] = y;
+                        if (a.out_bf16) static_cast<__nv_bfloat16 *>(a.out)[tt * a.ldo + m] = __float2bfloat16_rn(y);
+                        else static_cast<float *>(a.out)[tt * a.ldo + m] = y;
                     }
                 }
             }
             tc_fence_before();
             mbar_arrive(acc_empty);
         }
-    } else if (warp == 4) {
+    } else if (warp == kDecWarps) {
         // ------------------------------------------------------------ TMA (x)
         if (lane == 0) {
             int it = 0;
             bool go = true;
             pdl_wait();
             for (int tile = blockIdx.x; tile < ntiles && go; tile += gridDim.x) {
-                const int tn = tile % a.tiles_n;
+                const int tm = tile / a.tiles_n, tn = tile - tm * a.tiles_n;
                 for (int k = 0; k < nk; ++k, ++it) {
+                    if ((k & 1) == 0) {                       // packed tile of steps k, k+1
+                        const int pi = it >> 1, ps = pi % kPStages;
+                        if (pi >= kPStages &&
+                            !wait_or_abort(&empty_p[ps], ((pi / kPStages) - 1) & 1, abort_flag, a)) {
+                            go = false;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(&full_p[ps], kPBytes);
+                        tma_load_2d(sP + (size_t)ps * a128(kPBytes), &tmap_p, (k >> 1) * (int)kPRowBytes,
+                                    tm * kBM, &full_p[ps]);
+                    }
                     const int s = it % kStages;
                     if (it >= kStages && !wait_or_abort(&empty[s], ((it / kStages) - 1) & 1, abort_flag, a)) {
                         go = false;
@@ -262,6 +308,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_fixed(const __grid_constan
             for (int s = 0; s < kStages && s < it; ++s) {
                 const int last = it - 1 - ((it - 1 - s) % kStages);   // last step that used stage s
                 mbar_wait_bounded(&full_b[s], (last / kStages) & 1);
+            }
+            const int np = (it + 1) >> 1;                     // packed tiles issued
+            for (int s = 0; s < kPStages && s < np; ++s) {
+                const int last = np - 1 - ((np - 1 - s) % kPStages);
+                mbar_wait_bounded(&full_p[s], (last / kPStages) & 1);
             }
         }
     } else {
@@ -301,7 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_fixed(const __grid_constan
     // every role is done (or gave up): release the TMEM
     tc_fence_before();
     __syncthreads();
-    if (warp == 5) {
+    if (warp == kDecWarps + 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
     }
@@ -325,12 +376,17 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
+template <int BITS>
 size_t gemm_smem_bytes(uint32_t cb_entries) {
-    return 1024 + (size_t)kStages * (kABytes + kBBytes) + a128((size_t)cb_entries * 2) + 256;
+    return 1024 + (size_t)GemmCfg<BITS>::kStages * (kABytes + kBBytes) + kPStages * a128(GemmCfg<BITS>::kPBytes) +
+           a128((size_t)cb_entries * 2) + 256;
 }
 
 template <int BITS>
-int launch_gemm(const CUtensorMap &map, const GemmArgs &a, size_t smem, int grid, cudaStream_t s) {
+int launch_gemm(const CUtensorMap &map, const CUtensorMap &pmap, GemmArgs a, cudaStream_t s) {
+    const size_t smem = gemm_smem_bytes<BITS>(a.cb_entries);
+    if (smem > (size_t)cbq_host::max_smem_optin()) return CBQ_ERR_UNSUPPORTED;
+    const int grid = (int)std::min<int64_t>((int64_t)a.tiles_m * a.tiles_n, cbq_host::sm_count());
     auto kern = k_gemm_fixed<BITS>;
     static std::mutex mu;
     static size_t configured[64] = {0};
@@ -343,7 +399,7 @@ int launch_gemm(const CUtensorMap &map, const GemmArgs &a, size_t smem, int grid
             configured[dev & 63] = smem;
         }
     }
-    CBQ_CUDA_TRY(cbq_host::launch_pdl(kern, dim3(grid), dim3(kThreads), smem, s, map, a));
+    CBQ_CUDA_TRY(cbq_host::launch_pdl(kern, dim3(grid), dim3(kThreads), smem, s, map, pmap, a));
     return CBQ_OK;
 }
 
@@ -357,13 +413,11 @@ namespace cbq {
 int gemm_fixed(const void *x, int64_t T, int64_t ldx, const uint8_t *packed, const float *cb, int64_t C,
                int bits, int64_t M, int64_t K, const float *bias, void *out, int out_dtype, int64_t ldo,
                cudaStream_t s) {
-    if (bits < 1 || bits > 14 || M % kBM || K % kBK || K <= 0 || T <= 0 || M <= 0) return CBQ_ERR_UNSUPPORTED;
-    if ((reinterpret_cast<uintptr_t>(x) & 15) || (ldx * 2) % 16 || (reinterpret_cast<uintptr_t>(packed) & 3))
+    if (bits < 1 || bits > 14 || M % kBM || K % (2 * kBK) || K <= 0 || T <= 0 || M <= 0) return CBQ_ERR_UNSUPPORTED;
+    if ((reinterpret_cast<uintptr_t>(x) & 15) || (ldx * 2) % 16 || (reinterpret_cast<uintptr_t>(packed) & 15))
         return CBQ_ERR_UNSUPPORTED;
     if (M >= (1ll << 31) || T >= (1ll << 31) || K >= (1ll << 31)) return CBQ_ERR_UNSUPPORTED;
     const uint32_t entries = std::max<uint32_t>((uint32_t)C, 1u << bits);
-    const size_t smem = gemm_smem_bytes(entries);
-    if (smem > (size_t)cbq_host::max_smem_optin()) return CBQ_ERR_UNSUPPORTED;
     EncodeTiledFn enc = encode_fn();
     if (!enc) return CBQ_ERR_UNSUPPORTED;
     CUtensorMap map;
@@ -375,14 +429,24 @@ int gemm_fixed(const void *x, int64_t T, int64_t ldx, const uint8_t *packed, con
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return CBQ_ERR_UNSUPPORTED;
+    // the packed stream as a [M rows, K*bits/8 bytes] byte matrix; a box is
+    // 128 rows x 16*bits bytes = two K steps (16-byte multiple for every width)
+    CUtensorMap pmap;
+    const cuuint64_t row_bytes = (cuuint64_t)K * bits / 8;
+    const cuuint64_t pdims[2] = {row_bytes, (cuuint64_t)M};
+    const cuuint64_t pstrides[1] = {row_bytes};
+    const cuuint32_t pbox[2] = {(cuuint32_t)(16 * bits), (cuuint32_t)kBM};
+    if (enc(&pmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(packed), pdims, pstrides, pbox, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return CBQ_ERR_UNSUPPORTED;
     GemmArgs a{};
     a.packed = packed; a.codebook = cb; a.C = (int)C; a.bits = bits;
     a.M = (int)M; a.K = (int)K; a.T = (int)T; a.bias = bias; a.out = out; a.ldo = ldo;
     a.out_bf16 = out_dtype == CBQ_BF16; a.tiles_m = (int)(M / kBM); a.tiles_n = (int)((T + kBN - 1) / kBN);
     a.cb_entries = entries; a.status = nullptr;
-    const int grid = (int)std::min<int64_t>((int64_t)a.tiles_m * a.tiles_n, cbq_host::sm_count());
     switch (bits) {
-#define CBQ_G(n) case n: return launch_gemm<n>(map, a, smem, grid, s);
+#define CBQ_G(n) case n: return launch_gemm<n>(map, pmap, a, s);
         CBQ_G(1) CBQ_G(2) CBQ_G(3) CBQ_G(4) CBQ_G(5) CBQ_G(6) CBQ_G(7)
         CBQ_G(8) CBQ_G(9) CBQ_G(10) CBQ_G(11) CBQ_G(12) CBQ_G(13) CBQ_G(14)
 #undef CBQ_G

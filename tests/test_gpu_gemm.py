@@ -27,7 +27,7 @@ def _lin(dev, M, K, bits, seed, bf16_exact=True):
     return G.GPUAcceleratedLinear("w", packed, cb, (M, K), bits, device=dev), packed, cb
 
 
-@pytest.mark.parametrize("M,K,T,bits", [(128, 64, 64, 13), (256, 512, 300, 13), (512, 1024, 256, 8),
+@pytest.mark.parametrize("M,K,T,bits", [(128, 128, 64, 13), (256, 512, 300, 13), (512, 1024, 256, 8),
                                         (384, 256, 520, 4), (128, 4096, 96, 14)])
 def test_gemm_matches_oracle(M, K, T, bits):
     dev = need_cuda()
