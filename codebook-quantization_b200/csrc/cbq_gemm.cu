@@ -120,6 +120,35 @@ __device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
     return v;
 }
 
+// NW consecutive 32-bit words from shared address `addr`, whose offset from
+// a 16-byte boundary is OFF bytes (known at compile time): the widest
+// aligned loads, so lanes reading rows 16*b bytes apart hit few banks.
+template <int NW, int OFF>
+__device__ __forceinline__ void lds_words(uint32_t addr, uint32_t (&w)[NW + 1]) {
+    int j = 0;
+    int off = OFF;
+#pragma unroll
+    for (int it = 0; it < NW; ++it) {
+        if (j >= NW) break;
+        if (off % 16 == 0 && j + 4 <= NW) {
+            uint32_t a0, a1, a2, a3;
+            asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(a0), "=r"(a1), "=r"(a2), "=r"(a3) : "r"(addr));
+            w[j] = a0; w[j + 1] = a1; w[j + 2] = a2; w[j + 3] = a3;
+            j += 4; addr += 16; off += 16;
+        } else if (off % 8 == 0 && j + 2 <= NW) {
+            uint32_t a0, a1;
+            asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(a0), "=r"(a1) : "r"(addr));
+            w[j] = a0; w[j + 1] = a1;
+            j += 2; addr += 8; off += 8;
+        } else {
+            uint32_t a0;
+            asm volatile("ld.shared.u32 %0, [%1];" : "=r"(a0) : "r"(addr));
+            w[j] = a0;
+            j += 1; addr += 4; off += 4;
+        }
+    }
+}
+
 template <int BITS>
 __device__ __forceinline__ uint32_t field32(const uint32_t (&w)[BITS + 1], int i) {
     const int bit = i * BITS, wi = bit >> 5, sh = bit & 31;
@@ -215,13 +244,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_fixed(const __grid_constan
                     go = false;
                     break;
                 }
+                // set g reads the step k with k & 1 == g, warp-uniform h: the
+                // offset's alignment class is fixed per warp
                 const uint32_t pw = smem_u32(sP + (size_t)ps * a128(kPBytes)) + (uint32_t)r * kPRowBytes +
                                     (uint32_t)(k & 1) * (8u * BITS) + (uint32_t)h * (4u * BITS);
-#pragma unroll
-                for (int j = 0; j < NW; ++j) {
-                    uint32_t v;
-                    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(pw + 4u * j));
-                    w[j] = v;
+                constexpr int O1 = (4 * BITS) % 16, O2 = (8 * BITS) % 16, O3 = (12 * BITS) % 16;
+                switch ((k & 1) * 2 + h) {
+                    case 0: lds_words<NW, 0>(pw, w); break;
+                    case 1: lds_words<NW, O1>(pw, w); break;
+                    case 2: lds_words<NW, O2>(pw, w); break;
+                    default: lds_words<NW, O3>(pw, w); break;
                 }
                 w[NW] = 0u;
                 mbar_arrive(&empty_p[ps]);                    // words are in registers
