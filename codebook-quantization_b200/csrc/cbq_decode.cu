@@ -127,64 +127,118 @@ __global__ void __launch_bounds__(256) k_qk_norm_rope(const T *q, const T *k, co
 }
 
 // -------------------------------------------------------- decode attention
-// One CTA (D threads, D = head dim) per (row b, query head h): scores of keys
-// 0..pos, softmax, weighted sum of values, all in fp32.
-template <typename T, int D>
+// One CTA per (row b, kv head g) computes the G = Hq/Hkv query heads that
+// share the kv head, so every K and V row is read once.  D threads; keys are
+// processed in batches of 8 per warp with independent loads (the cache reads
+// are latency-bound at decode sizes), scores of all G heads live in shared
+// memory, softmax and the weighted sum of values run in fp32.
+template <typename T, int D, int G>
 __global__ void __launch_bounds__(D) k_attn_decode(const T *q, const T *k_cache, const T *v_cache,
                                                    const int64_t *pos_dev, int Hq, int Hkv, int64_t L,
                                                    float scale, T *out) {
-    constexpr int NW = D / 32, E = D / 32;
-    extern __shared__ float sc[];                 // scores [L]
-    __shared__ float red[32];
+    constexpr int NW = D / 32, E = D / 32, KB = 8;
+    extern __shared__ float sc[];                 // scores [G][L]
+    __shared__ float red[G][NW];
+    __shared__ float stat[G][2];                  // max, sum
     pdl_launch_dependents();
     pdl_wait();
-    const int bh = blockIdx.x;
-    const int b = bh / Hq, h = bh - b * Hq;
-    const int g = h / (Hq / Hkv);
+    const int bg = blockIdx.x;
+    const int b = bg / Hkv, g = bg - b * Hkv;
     const int64_t n = min(*pos_dev + 1, L);            // keys 0..pos (none if pos < 0)
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const T *qr = q + ((int64_t)b * Hq + h) * D;
-    float qv[E];
+    float qv[G][E];
 #pragma unroll
-    for (int e = 0; e < E; ++e) qv[e] = ld(qr, lane * E + e);
+    for (int h = 0; h < G; ++h) {
+        const T *qr = q + ((int64_t)b * Hq + g * G + h) * D;
+#pragma unroll
+        for (int e = 0; e < E; ++e) qv[h][e] = ld(qr, lane * E + e);
+    }
     const T *kb = k_cache + ((int64_t)b * Hkv + g) * L * D;
     const T *vb = v_cache + ((int64_t)b * Hkv + g) * L * D;
-    float mx = -INFINITY;
-    for (int64_t j = warp; j < n; j += NW) {
-        const T *kr = kb + j * D + lane * E;
-        float d = 0.f;
+    float mx[G];
 #pragma unroll
-        for (int e = 0; e < E; ++e) d += qv[e] * ld(kr, e);
-        d = warp_sum(d) * scale;
-        if (lane == 0) sc[j] = d;
-        mx = fmaxf(mx, d);
-    }
-    if (lane == 0) red[warp] = mx;
-    __syncthreads();
-    mx = -INFINITY;
+    for (int h = 0; h < G; ++h) mx[h] = -INFINITY;
+    for (int64_t j0 = (int64_t)warp * KB; j0 < n; j0 += (int64_t)NW * KB) {
+        float kv[KB][E];
 #pragma unroll
-    for (int w = 0; w < NW; ++w) mx = fmaxf(mx, red[w]);
+        for (int u = 0; u < KB; ++u) {                // KB independent row loads
+            const int64_t j = min(j0 + u, n - 1);
+#pragma unroll
+            for (int e = 0; e < E; ++e) kv[u][e] = ld(kb, j * D + lane * E + e);
+        }
+#pragma unroll
+        for (int u = 0; u < KB; ++u) {
+#pragma unroll
+            for (int h = 0; h < G; ++h) {
+                float d = 0.f;
+#pragma unroll
+                for (int e = 0; e < E; ++e) d += qv[h][e] * kv[u][e];
+                d = warp_sum(d) * scale;
+                if (j0 + u < n) {
+                    if (lane == 0) sc[h * L + j0 + u] = d;
+                    mx[h] = fmaxf(mx[h], d);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int h = 0; h < G; ++h)
+        if (lane == 0) red[h][warp] = mx[h];
     __syncthreads();
-    float sum = 0.f;
-    for (int64_t j = threadIdx.x; j < n; j += D) {
-        const float p = expf(sc[j] - mx);
-        sc[j] = p;
-        sum += p;
+    if (threadIdx.x < G) {
+        float m = -INFINITY;
+        for (int w = 0; w < NW; ++w) m = fmaxf(m, red[threadIdx.x][w]);
+        stat[threadIdx.x][0] = m;
     }
-    sum = block_sum<D>(sum, red);            // includes the barrier that publishes sc[]
-    if (n <= 0) {
-        out[((int64_t)b * Hq + h) * D + threadIdx.x] = from_f32<T>(0.f);
-        return;
+    __syncthreads();
+    float sum[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+        sum[h] = 0.f;
+        const float m = stat[h][0];
+        for (int64_t j = threadIdx.x; j < n; j += D) {
+            const float p = expf(sc[h * L + j] - m);
+            sc[h * L + j] = p;
+            sum[h] += p;
+        }
+        sum[h] = warp_sum(sum[h]);
     }
-    float acc0 = 0.f, acc1 = 0.f;
+    __syncthreads();                                  // red[] reuse; sc[] published below
+#pragma unroll
+    for (int h = 0; h < G; ++h)
+        if (lane == 0) red[h][warp] = sum[h];
+    __syncthreads();
+    if (threadIdx.x < G) {
+        float t = 0.f;
+        for (int w = 0; w < NW; ++w) t += red[threadIdx.x][w];
+        stat[threadIdx.x][1] = t;
+    }
+    __syncthreads();
+    // out[h][i] = sum_j p_h[j] v[j][i]: thread i, KB independent value loads per step
     const int i = threadIdx.x;
+    float acc[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) acc[h] = 0.f;
     int64_t j = 0;
-    for (; j + 1 < n; j += 2) {
-        acc0 = fmaf(sc[j], ld(vb, j * D + i), acc0);
-        acc1 = fmaf(sc[j + 1], ld(vb, (j + 1) * D + i), acc1);
+    for (; j + KB <= n; j += KB) {
+        float vv[KB];
+#pragma unroll
+        for (int u = 0; u < KB; ++u) vv[u] = ld(vb, (j + u) * D + i);
+#pragma unroll
+        for (int u = 0; u < KB; ++u)
+#pragma unroll
+            for (int h = 0; h < G; ++h) acc[h] = fmaf(sc[h * L + j + u], vv[u], acc[h]);
     }
-    if (j < n) acc0 = fmaf(sc[j], ld(vb, j * D + i), acc0);
-    out[((int64_t)b * Hq + h) * D + i] = from_f32<T>((acc0 + acc1) / sum);
+    for (; j < n; ++j) {
+        const float v = ld(vb, j * D + i);
+#pragma unroll
+        for (int h = 0; h < G; ++h) acc[h] = fmaf(sc[h * L + j], v, acc[h]);
+    }
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+        const float tot = stat[h][1];
+        out[((int64_t)b * Hq + g * G + h) * D + i] = from_f32<T>(n > 0 ? acc[h] / tot : 0.f);
+    }
 }
 
 }  // namespace
@@ -248,28 +302,46 @@ extern "C" int cbq_attn_decode(const void *q_dev, const void *k_cache_dev, const
     if (B < 0 || Hq < 1 || Hkv < 1 || Hq % Hkv || cache_len < 1 || (dtype != CBQ_F32 && dtype != CBQ_BF16))
         return CBQ_ERR_ARG;
     if (head_dim != 64 && head_dim != 128 && head_dim != 256) return CBQ_ERR_UNSUPPORTED;
-    if (cache_len > 32768) return CBQ_ERR_UNSUPPORTED;           // scores live in shared memory
+    const int64_t G = Hq / Hkv;
+    if (G < 1 || G > 8) return CBQ_ERR_UNSUPPORTED;
+    const size_t smem = (size_t)cache_len * 4 * (size_t)G;       // scores of the group's heads
+    if (smem > (size_t)cbq_host::max_smem_optin() - 4096) return CBQ_ERR_UNSUPPORTED;
     if (B == 0) return CBQ_OK;
-    if (!q_dev || !k_cache_dev || !v_cache_dev || !pos_dev || !out_dev || B * Hq > 0x7fffffff) return CBQ_ERR_ARG;
-    const size_t smem = (size_t)cache_len * 4;
+    if (!q_dev || !k_cache_dev || !v_cache_dev || !pos_dev || !out_dev || B * Hkv > 0x7fffffff) return CBQ_ERR_ARG;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-#define CBQ_AT(T, D)                                                                                 \
+    const dim3 grid((unsigned)(B * Hkv));
+#define CBQ_AT(T, D, GG)                                                                             \
     do {                                                                                             \
         if (smem > 48 * 1024)                                                                        \
-            CBQ_CUDA_TRY(cudaFuncSetAttribute(k_attn_decode<T, D>,                                   \
+            CBQ_CUDA_TRY(cudaFuncSetAttribute(k_attn_decode<T, D, GG>,                               \
                                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
-        CBQ_CUDA_TRY(cbq_host::launch_pdl(k_attn_decode<T, D>, dim3((unsigned)(B * Hq)), dim3(D), smem, s, \
+        CBQ_CUDA_TRY(cbq_host::launch_pdl(k_attn_decode<T, D, GG>, grid, dim3(D), smem, s,           \
                                           static_cast<const T *>(q_dev), static_cast<const T *>(k_cache_dev), \
                                           static_cast<const T *>(v_cache_dev), pos_dev, (int)Hq, (int)Hkv, \
                                           cache_len, scale, static_cast<T *>(out_dev)));             \
     } while (0)
+#define CBQ_AT_G(T, D)                                                                               \
+    do {                                                                                             \
+        switch (G) {                                                                                 \
+            case 1: CBQ_AT(T, D, 1); break;                                                          \
+            case 2: CBQ_AT(T, D, 2); break;                                                          \
+            case 3: CBQ_AT(T, D, 3); break;                                                          \
+            case 4: CBQ_AT(T, D, 4); break;                                                          \
+            case 5: CBQ_AT(T, D, 5); break;                                                          \
+            case 6: CBQ_AT(T, D, 6); break;                                                          \
+            case 7: CBQ_AT(T, D, 7); break;                                                          \
+            default: CBQ_AT(T, D, 8); break;                                                         \
+        }                                                                                            \
+    } while (0)
     if (dtype == CBQ_F32) {
-        if (head_dim == 64) CBQ_AT(float, 64); else if (head_dim == 128) CBQ_AT(float, 128); else CBQ_AT(float, 256);
+        if (head_dim == 64) CBQ_AT_G(float, 64); else if (head_dim == 128) CBQ_AT_G(float, 128);
+        else CBQ_AT_G(float, 256);
     } else {
-        if (head_dim == 64) CBQ_AT(__nv_bfloat16, 64);
-        else if (head_dim == 128) CBQ_AT(__nv_bfloat16, 128);
-        else CBQ_AT(__nv_bfloat16, 256);
+        if (head_dim == 64) CBQ_AT_G(__nv_bfloat16, 64);
+        else if (head_dim == 128) CBQ_AT_G(__nv_bfloat16, 128);
+        else CBQ_AT_G(__nv_bfloat16, 256);
     }
+#undef CBQ_AT_G
 #undef CBQ_AT
     CBQ_CUDA_TRY(cudaGetLastError());
     return CBQ_OK;

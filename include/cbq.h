@@ -291,7 +291,9 @@ int cbq_qk_norm_rope(const void *q_dev, const void *k_dev, const void *v_dev, in
 /* Grouped-query attention of q [B, Hq, d] over cache rows 0..*pos_dev of
  * k_cache / v_cache [B, Hkv, cache_len, d] (query head h reads kv head
  * h / (Hq / Hkv)), softmax(q k^T * scale) v in fp32 -> out [B, Hq*d].
- * cache_len <= 32768. */
+ * Hq / Hkv <= 8; the scores of one kv head's query heads
+ * (cache_len * Hq/Hkv * 4 bytes) are held in shared memory, so longer caches
+ * return CBQ_ERR_UNSUPPORTED. */
 int cbq_attn_decode(const void *q_dev, const void *k_cache_dev, const void *v_cache_dev, int dtype,
                     int64_t B, int64_t Hq, int64_t Hkv, int64_t head_dim, int64_t cache_len,
                     const int64_t *pos_dev, float scale, void *out_dev, void *stream);
