@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--shape", default="12288,4096", help="gemv workload: M,K")
     ap.add_argument("--tokens", type=int, default=1, help="gemv workload: T (activation rows)")
     ap.add_argument("--x-dtype", default="bf16", choices=["bf16", "f32"], help="gemv workload: activation dtype")
+    ap.add_argument("--allreduce", default="peer", choices=["peer", "nccl"],
+                    help="tensor parallelism: fused peer-memory all-reduce or NCCL")
     return ap.parse_args()
 
 
@@ -342,7 +344,8 @@ def main():
     H = cfg.hidden
     prompt_len = 64
     max_len = prompt_len + args.warmup + 2 * args.steps + 8
-    dec = qd.Qwen3Decoder(W, batch=args.batch, max_len=max_len, act_dtype=torch.bfloat16, group=group)
+    dec = qd.Qwen3Decoder(W, batch=args.batch, max_len=max_len, act_dtype=torch.bfloat16, group=group,
+                          allreduce=args.allreduce)
     g = torch.Generator().manual_seed(1234)
     prompt = torch.randint(0, cfg.vocab, (args.batch, prompt_len), generator=g)
     if not args.no_graph:
@@ -429,6 +432,8 @@ def main():
             "config": {"workload": f"{cfg.name} greedy decode, batch {args.batch}, "
                                    f"{'huffman' if args.huffman else 'fixed 13-bit'} streams, CUDA graph",
                        "global_batch": args.batch, "seq_len": max_len, "parallelism": f"tp{world}",
+                       "allreduce": ("peer-memory (GEMV epilogue + RMSNorm)" if dec.peer is not None
+                                     else ("nccl" if world > 1 else "none")),
                        "l2": "weights 12.3 GB >> 126 MB L2 (no flush)",
                        "stream_bytes_per_rank": stack_bytes,
                        "hbm_gbs_whole_step": stack_bytes / (ms_step * 1e-3) / 1e9,

@@ -34,6 +34,8 @@ SIGNATURES = {
                                 _INT, _I64, _P, _I64, _P]),
     "cbq_linear_fixed_multi": (_INT, [_P, _INT, _I64, _I64, _INT, _P, _P, _P, _P, _I64, _INT, _I64, _P,
                                       _P, _P, _P, _INT, _INT, _P]),
+    "cbq_linear_fixed_peer": (_INT, [_P, _INT, _I64, _I64, _P, _I64, _P, _I64, _INT, _I64, _I64, _P, _INT,
+                                     _P, _P, _I64, _INT, _P]),
     "cbq_linear_fixed_noalloc": (_INT, [_P, _INT, _I64, _I64, _P, _I64, _P, _I64, _INT, _I64, _I64, _P,
                                         _P, _INT, _I64, _P]),
     "cbq_embedding_fixed": (_INT, [_P, _I64, _P, _I64, _P, _I64, _INT, _I64, _I64, _P, _INT, _P, _P]),
@@ -54,6 +56,8 @@ SIGNATURES = {
     "cbq_huff_decode_indices": (_INT, [_P, _I64, _P, _P, _P, _I64, _I64, _P, _P, _P]),
     "cbq_huff_encode": (_INT, [_P, _I64, _P, _P, _P, _P, _I64, _P]),
     "cbq_rmsnorm": (_INT, [_P, _P, _INT, _I64, _I64, _P, ct.c_float, _P, _P]),
+    "cbq_rmsnorm_allreduce": (_INT, [_P, _P, _P, _P, _I64, _INT, _INT, _I64, _I64, _P, ct.c_float, _P, _P,
+                                     _P]),
     "cbq_qk_norm_rope": (_INT, [_P, _P, _P, _INT, _I64, _I64, _I64, _I64, ct.c_float, _P, _P, _P, _P, _P,
                                 _P, _P, _P, _I64, _P]),
     "cbq_attn_decode": (_INT, [_P, _P, _P, _INT, _I64, _I64, _I64, _I64, _I64, _P, ct.c_float, _P, _P]),

@@ -65,6 +65,64 @@ __global__ void __launch_bounds__(NT) k_rmsnorm(T *x, const T *add, int64_t n, c
     }
 }
 
+// -------------------------------------- all-reduce + residual + RMSNorm
+// The consumer of the peer-partial GEMV epilogue: wait until every rank s has
+// delivered its partial rows to slot s (counts[s] >= epoch * expect; bounded,
+// %globaltimer), then x[r] = round(x[r] + round(sum_s slot[s][r])) in rank
+// order (every rank computes the same values) and out[r] = RMSNorm(x[r]).
+template <typename T, int NT>
+__global__ void __launch_bounds__(NT) k_rmsnorm_allreduce(T *x, const T *slots, const uint32_t *counts,
+                                                          const uint32_t *epoch, uint32_t expect, int world,
+                                                          int64_t rows, int64_t n, const float *w, float eps,
+                                                          T *out, uint32_t *status) {
+    __shared__ float red[32];
+    __shared__ int late;
+    pdl_launch_dependents();
+    pdl_wait();
+    // a wait that already gave up in this run: do not wait again
+    if (threadIdx.x == 0) late = (status && (*(volatile uint32_t *)(status + CBQ_STATUS_FLAGS) & CBQ_FLAG_TIMEOUT)) ? 1 : 0;
+    __syncthreads();
+    if (late) return;
+    if (threadIdx.x < world) {
+        const uint32_t want = *epoch * expect;
+        const uint64_t t0 = global_timer_ns();
+        while (true) {
+            uint32_t c;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(c) : "l"(counts + threadIdx.x) : "memory");
+            if ((int32_t)(c - want) >= 0) break;
+            if (global_timer_ns() - t0 > kWaitNs) {
+                late = 1;
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    __syncthreads();
+    if (late) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) report(status, CBQ_FLAG_TIMEOUT, 0u);
+        return;
+    }
+    __threadfence_system();
+    const int64_t r = blockIdx.x;
+    T *xr = x + r * n;
+    T *orow = out + r * n;
+    float ss = 0.f;
+    for (int64_t i = threadIdx.x; i < n; i += NT) {
+        float sum = 0.f;
+        for (int p = 0; p < world; ++p) sum += ld(slots, ((int64_t)p * rows + r) * n + i);
+        const float v = rnd<T>(ld(xr, i) + rnd<T>(sum));
+        xr[i] = from_f32<T>(v);
+        ss += v * v;
+    }
+    const float tot = block_sum<NT>(ss, red);
+    const float scale = rsqrtf(tot / (float)n + eps);
+    for (int64_t i = threadIdx.x; i < n; i += NT) {
+        float v = rnd<T>(ld(xr, i) * scale);
+        if (w) v = w[i] * v;
+        orow[i] = from_f32<T>(v);
+    }
+}
+
 // ------------------------------------------- q/k norm + rope + cache write
 // One warp per head: heads [0, Hq) of q, then Hkv of k, then Hkv of v, for
 // each of B rows.  Lane l holds elements [l*E, l*E + E) with E = d/32;
@@ -260,6 +318,30 @@ extern "C" int cbq_rmsnorm(void *x_dev, const void *add_dev, int dtype, int64_t 
                                           static_cast<__nv_bfloat16 *>(x_dev),
                                           static_cast<const __nv_bfloat16 *>(add_dev), n, weight_dev, eps,
                                           static_cast<__nv_bfloat16 *>(out_dev)));
+    return CBQ_OK;
+}
+
+extern "C" int cbq_rmsnorm_allreduce(void *x_dev, const void *slots_dev, const uint32_t *counts_dev,
+                                     const uint32_t *epoch_dev, int64_t expect, int world, int dtype, int64_t rows,
+                                     int64_t n, const float *weight_dev, float eps, void *out_dev,
+                                     uint32_t *status_dev, void *stream) {
+    if (rows < 0 || n < 1 || world < 1 || world > 32 || expect < 1 || expect > 0xffffffffll ||
+        (dtype != CBQ_F32 && dtype != CBQ_BF16))
+        return CBQ_ERR_ARG;
+    if (rows == 0) return CBQ_OK;
+    if (!x_dev || !slots_dev || !counts_dev || !epoch_dev || !out_dev || rows > 0x7fffffff) return CBQ_ERR_ARG;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (dtype == CBQ_F32)
+        CBQ_CUDA_TRY(cbq_host::launch_pdl(k_rmsnorm_allreduce<float, 256>, dim3((unsigned)rows), dim3(256), 0, s,
+                                          static_cast<float *>(x_dev), static_cast<const float *>(slots_dev),
+                                          counts_dev, epoch_dev, (uint32_t)expect, world, rows, n, weight_dev,
+                                          eps, static_cast<float *>(out_dev), status_dev));
+    else
+        CBQ_CUDA_TRY(cbq_host::launch_pdl(k_rmsnorm_allreduce<__nv_bfloat16, 256>, dim3((unsigned)rows), dim3(256),
+                                          0, s, static_cast<__nv_bfloat16 *>(x_dev),
+                                          static_cast<const __nv_bfloat16 *>(slots_dev), counts_dev, epoch_dev,
+                                          (uint32_t)expect, world, rows, n, weight_dev, eps,
+                                          static_cast<__nv_bfloat16 *>(out_dev), status_dev));
     return CBQ_OK;
 }
 

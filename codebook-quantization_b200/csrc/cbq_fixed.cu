@@ -162,6 +162,11 @@ bool plan_gemv(int64_t M, int64_t K, int bits, int64_t C, int64_t T, GemvPlan &p
     if (fixed + a128((size_t)NP * 4) > budget) return false;
     int64_t H = (int64_t)((budget - fixed - 128 - (size_t)NP * 4) / 124);
     H = std::min<int64_t>(H, C);
+    // The replicated head costs 128 bytes of shared-memory stores per entry in
+    // every CTA; for a small share of the stream per CTA those stores cost more
+    // than the bank conflicts they save, so the head shrinks with the share.
+    const int64_t cta_bytes = rows * K * bits / 8;
+    H = std::min<int64_t>(H, std::max<int64_t>(64, cta_bytes / 256));
     p.grid = (int)((M + rows - 1) / rows);
     p.rows_per_cta = (int)rows;
     p.nseg = nseg;
@@ -323,6 +328,40 @@ extern "C" int cbq_linear_fixed_multi(const void *x_dev, int x_dtype, int64_t T,
                            resid_dev ? resid_dev[m] : nullptr, ldo[m], (int)M[m]};
     a.out_bf16 = out_dtype == CBQ_BF16;
     a.H = g.H; a.NP = g.NP; a.m128 = 128u; a.m4 = 4u; a.status = nullptr;
+    return launch_gemv(bits, (int)T, g.nf, x_dtype == CBQ_BF16, a, g.smem, g.grid,
+                       static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int cbq_linear_fixed_peer(const void *x_dev, int x_dtype, int64_t T, int64_t ldx,
+                                     const uint8_t *packed_dev, int64_t packed_bytes, const float *codebook_dev,
+                                     int64_t C, int bits, int64_t M, int64_t K, const float *bias_dev, int world,
+                                     void *const *slot_dev, uint32_t *const *count_dev, int64_t ldo, int out_dtype,
+                                     void *stream) {
+    if (world < 1 || world > kGvMaxPeers || !slot_dev || !count_dev) return CBQ_ERR_ARG;
+    if (T < 1 || M < 1 || K < 1 || bits < 1 || bits > 16 || C < 1 || C > 65536 || ldo < M) return CBQ_ERR_ARG;
+    if ((x_dtype != CBQ_F32 && x_dtype != CBQ_BF16) || (out_dtype != CBQ_F32 && out_dtype != CBQ_BF16))
+        return CBQ_ERR_ARG;
+    if (!x_dev || !packed_dev || !codebook_dev || ldx < K) return CBQ_ERR_ARG;
+    if (packed_bytes < cbq_fixed_stream_bytes(M, K, bits)) return CBQ_ERR_ARG;
+    for (int p = 0; p < world; ++p)
+        if (!slot_dev[p] || !count_dev[p]) return CBQ_ERR_ARG;
+    const int xbytes = x_dtype == CBQ_BF16 ? 2 : 4;
+    if ((reinterpret_cast<uintptr_t>(x_dev) & 15) || (ldx * xbytes) % 16 || (reinterpret_cast<uintptr_t>(packed_dev) & 15))
+        return CBQ_ERR_UNSUPPORTED;
+    GemvPlan g;
+    if (!plan_gemv(M, K, bits, C, T, g)) return CBQ_ERR_UNSUPPORTED;
+    GemvArgs a{};
+    a.x = x_dev; a.ldx = ldx; a.t0 = 0; a.ntok = (int)T; a.codebook = codebook_dev;
+    a.C = (int)C; a.M = (int)M; a.K = (int)K; a.nseg = g.nseg; a.rows_per_cta = g.rows_per_cta;
+    a.nmat = 1; a.epi = kEpiPeer;
+    a.mat[0] = GemvMat{packed_dev, nullptr, bias_dev, nullptr, ldo, (int)M};
+    a.out_bf16 = out_dtype == CBQ_BF16;
+    a.H = g.H; a.NP = g.NP; a.m128 = 128u; a.m4 = 4u; a.status = nullptr;
+    a.peers.world = world;
+    for (int p = 0; p < world; ++p) {
+        a.peers.slot[p] = slot_dev[p];
+        a.peers.count[p] = count_dev[p];
+    }
     return launch_gemv(bits, (int)T, g.nf, x_dtype == CBQ_BF16, a, g.smem, g.grid,
                        static_cast<cudaStream_t>(stream));
 }

@@ -70,6 +70,19 @@ enum GemvEpi : int {
     kEpiStore = 0,       // out = acc (+ bias)
     kEpiResidual = 1,    // out = resid + round(acc + bias)      (the residual stream update)
     kEpiSiluMul = 2,     // two matrices of equal M: out0 = round(silu(round(g)) * round(u))
+    kEpiPeer = 3,        // tensor parallelism: the partial product goes to every rank's slot
+};
+
+constexpr int kGvMaxPeers = 8;
+
+// kEpiPeer: rank s's partial rows go to slot s of every rank's all-reduce
+// buffer (peer memory over NVLink), then every CTA adds its row count to
+// each rank's arrival counter for slot s (system-scope release); the
+// consumer (cbq_rmsnorm_allreduce) waits for the counters and sums the slots.
+struct GemvPeers {
+    void *slot[kGvMaxPeers];          // rank p's slot for this rank, [T, ldo] in the output dtype
+    uint32_t *count[kGvMaxPeers];     // rank p's arrival counter for this rank
+    int world;
 };
 
 struct GemvArgs {
@@ -89,6 +102,7 @@ struct GemvArgs {
     uint32_t NP;         // entries held in shared memory (head + single copy)
     uint32_t m128, m4;   // 128 and 4
     uint32_t *status;
+    GemvPeers peers;     // kEpiPeer only
 };
 
 // Row v of the launch's row space -> (matrix, row of that matrix).  Rows are
@@ -417,6 +431,26 @@ __global__ void __launch_bounds__(kGvWarps * 32, 1) k_gemv_fixed(const GemvArgs 
                 store(g, (a.t0 + t) * g.ldo + row, sv * uv);
             }
         }
+    } else if (a.epi == kEpiPeer) {
+        const GemvMat &mt = a.mat[0];
+        for (int r = tid; r < nrows; r += kGvWarps * 32) {
+            const int64_t row = m0 + r;
+            const float b = mt.bias ? mt.bias[row] : 0.f;
+            for (int t = 0; t < a.ntok; ++t) {
+                const int64_t o = (a.t0 + t) * mt.ldo + row;
+                const float v = seg_sum(r, t) + b;
+                for (int p = 0; p < a.peers.world; ++p) {
+                    if (a.out_bf16) static_cast<__nv_bfloat16 *>(a.peers.slot[p])[o] = __float2bfloat16_rn(v);
+                    else static_cast<float *>(a.peers.slot[p])[o] = v;
+                }
+            }
+        }
+        // The barrier orders every thread's peer stores before the counter
+        // updates, and a system-scope release is cumulative over them.
+        __syncthreads();
+        if (tid < a.peers.world)
+            asm volatile("red.release.sys.global.add.u32 [%0], %1;"
+                         ::"l"(a.peers.count[tid]), "r"((uint32_t)nrows) : "memory");
     } else {
         for (int r = tid; r < nrows; r += kGvWarps * 32) {
             int64_t row;

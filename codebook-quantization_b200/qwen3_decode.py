@@ -42,6 +42,62 @@ from .qwen3 import CompressedQwen3Weights
 __all__ = ["Qwen3Decoder", "rope_tables"]
 
 
+class _PeerAllReduce:
+    """The row-parallel layers' all-reduce over NVLink peer memory.
+
+    One symmetric buffer per decoder: for every all-reduce site (o_proj and
+    down_proj of each layer) a slot per rank ([world][B][hidden] in the
+    activation dtype) and an arrival counter per rank.  Rank s's GEMV writes
+    its partial product into slot s of every rank and adds its rows to every
+    rank's counter s (``cbq_linear_fixed_peer``); each rank's
+    ``cbq_rmsnorm_allreduce`` waits for epoch * hidden rows from every rank,
+    adds the slots in rank order into the residual stream and normalises.
+    Counters only grow (``epoch`` counts the steps), so nothing is reset
+    between steps."""
+
+    def __init__(self, dec, sites: int):
+        import ctypes as ct
+        import torch.distributed._symmetric_memory as symm
+        self.dec = dec
+        W, r = dec.world, dec.rank
+        self.W, self.rank = W, r
+        self.n = dec.B * dec.cfg.hidden
+        self.elem = 2 if dec.dt == torch.bfloat16 else 4
+        self.slot_bytes = self.n * self.elem           # the consumer reads the slots back to back
+        if self.slot_bytes % 16:
+            raise ValueError("batch * hidden must fill whole 16-byte units")
+        data = sites * W * self.slot_bytes
+        total = data + ((sites * W * 4 + 127) // 128) * 128
+        self.buf = symm.empty(total, dtype=torch.uint8, device=dec.dev)
+        self.buf.zero_()
+        self.hdl = symm.rendezvous(self.buf, dec.group)
+        ptrs = list(self.hdl.buffer_ptrs)
+        self.local = self.buf.data_ptr()
+        self.data = data
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=dec.dev)
+        self.status = torch.zeros(4, dtype=torch.int32, device=dec.dev)
+        self.slots, self.counts = [], []
+        P = ct.c_void_p
+        for i in range(sites):
+            self.slots.append((P * W)(*[ptrs[p] + (i * W + r) * self.slot_bytes for p in range(W)]))
+            self.counts.append((P * W)(*[ptrs[p] + data + (i * W + r) * 4 for p in range(W)]))
+        torch.cuda.synchronize(dec.dev)
+        dist.barrier(group=dec.group)
+
+    def run(self, site: int, lin, x):
+        dec = self.dec
+        W = self.W
+        stream = device_stream(dec.dev)
+        rc = _lib.lib().cbq_linear_fixed_peer(
+            x.data_ptr(), dec.code, dec.B, x.shape[1], lin.packed.data_ptr(), lin.nbytes, lin.codebook.data_ptr(),
+            lin.C, lin.bits, lin.M, lin.K, None, W, self.slots[site], self.counts[site], lin.M, dec.code, stream)
+        if rc != _lib.CBQ_OK:
+            raise _lib.CbqError("cbq_linear_fixed_peer", rc)
+        _lib.call("cbq_rmsnorm_allreduce", dec.x.data_ptr(), self.local + site * W * self.slot_bytes,
+                  self.local + self.data + site * W * 4, self.epoch.data_ptr(), lin.M, W, dec.code, dec.B,
+                  dec.cfg.hidden, None, float(dec.cfg.rms_eps), dec.h.data_ptr(), self.status.data_ptr(), stream)
+
+
 def rope_tables(head_dim: int, max_len: int, theta: float, device):
     """cos/sin [max_len, head_dim] in fp32, HF's default rotary layout,
     computed on the host (as HF does on a CPU model) and copied to ``device``."""
@@ -66,7 +122,8 @@ def _rms(x, eps):
 
 class Qwen3Decoder:
     def __init__(self, weights: CompressedQwen3Weights, batch: int, max_len: int,
-                 act_dtype=torch.bfloat16, group: Optional[dist.ProcessGroup] = None, fused: bool = True):
+                 act_dtype=torch.bfloat16, group: Optional[dist.ProcessGroup] = None, fused: bool = True,
+                 allreduce: str = "peer"):
         self.w, self.cfg = weights, weights.cfg
         cfg = self.cfg
         self.dev = weights.device
@@ -99,6 +156,9 @@ class Qwen3Decoder:
             self.qn, self.a = z(hq), z(hq)
             self.m = z(cfg.inter // self.world)
             self.code = _lib.CBQ_BF16 if act_dtype == torch.bfloat16 else _lib.CBQ_F32
+        self.peer = None
+        if fused and self.world > 1 and allreduce == "peer" and not weights.huffman and batch <= 2:
+            self.peer = _PeerAllReduce(self, 2 * cfg.layers)
         L = weights.layers
         self.emb = L["model.embed_tokens.weight"]
         self.lm_head = L["lm_head.weight"]
@@ -164,6 +224,8 @@ class Qwen3Decoder:
     def _step_fused(self):
         cfg, B, d, dt = self.cfg, self.B, self.cfg.head_dim, self.dt
         stream = device_stream(self.dev)
+        if self.peer is not None:
+            self.peer.epoch.add_(1)
         self.emb(self.ids, out=self.x)
         self._rmsnorm(self.x, self.h)
         for li, (q_p, k_p, v_p, o_p, g_p, u_p, d_p) in enumerate(self.layer_mods):
@@ -178,6 +240,8 @@ class Qwen3Decoder:
             if self.world == 1:
                 self._linear((o_p,), (self.x,), _lib.CBQ_EPI_RESIDUAL, (self.x,), x=self.a)
                 self._rmsnorm(self.x, self.h)
+            elif self.peer is not None:
+                self.peer.run(2 * li, o_p, self.a)
             else:
                 self._linear((o_p,), (self.y,), x=self.a)
                 self._allreduce(self.y)
@@ -186,6 +250,8 @@ class Qwen3Decoder:
             if self.world == 1:
                 self._linear((d_p,), (self.x,), _lib.CBQ_EPI_RESIDUAL, (self.x,), x=self.m)
                 self._rmsnorm(self.x, self.h)
+            elif self.peer is not None:
+                self.peer.run(2 * li + 1, d_p, self.m)
             else:
                 self._linear((d_p,), (self.y,), x=self.m)
                 self._allreduce(self.y)

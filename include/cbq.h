@@ -130,6 +130,22 @@ int cbq_linear_fixed_multi(const void *x_dev, int x_dtype, int64_t T, int64_t ld
                            const int64_t *ldo, const void *const *resid_dev, int out_dtype,
                            int epilogue, void *stream);
 
+/* Tensor-parallel row-parallel layer (o_proj, down_proj), fused with the
+ * data movement of its all-reduce: the GEMV of this rank's K-block writes its
+ * partial product [T, M] into every rank's slot for this rank
+ * (slot_dev[p]: device pointer into rank p's memory, e.g. a symmetric
+ * buffer, world <= 8), then each CTA adds its row count to every rank's
+ * arrival counter for this rank (count_dev[p], system-scope release), so the
+ * counters grow by M per call.  cbq_rmsnorm_allreduce is the consumer.  No
+ * counterpart in the reference (single device).  Host arrays of world
+ * pointers; T <= 2 and the alignment rules of cbq_linear_fixed_multi, else
+ * CBQ_ERR_UNSUPPORTED before launching. */
+int cbq_linear_fixed_peer(const void *x_dev, int x_dtype, int64_t T, int64_t ldx,
+                          const uint8_t *packed_dev, int64_t packed_bytes, const float *codebook_dev,
+                          int64_t C, int bits, int64_t M, int64_t K, const float *bias_dev, int world,
+                          void *const *slot_dev, uint32_t *const *count_dev, int64_t ldo, int out_dtype,
+                          void *stream);
+
 /* Size of the device array built into the library that
  * cbq_linear_fixed_noalloc uses as its workspace (8 MiB on every GPU that
  * loads the library, until the process exits). */
@@ -275,6 +291,18 @@ int cbq_huff_encode(const uint16_t *idx_dev, int64_t n, const uint32_t *code_dev
  * (fp32 [n]) or 1. */
 int cbq_rmsnorm(void *x_dev, const void *add_dev, int dtype, int64_t rows, int64_t n,
                 const float *weight_dev, float eps, void *out_dev, void *stream);
+
+/* The all-reduce consumer: waits (bounded, 2 s; CBQ_FLAG_TIMEOUT in
+ * status_dev, nothing written, on expiry) until counts_dev[s] >=
+ * (*epoch_dev) * expect for every rank s < world, then for each row r of x
+ * [rows, n]: x[r] = round(x[r] + round(sum_s slots[s][r])) in rank order
+ * (slots_dev: [world][rows][n], this rank's buffer that the peers wrote) and
+ * out[r] = RMSNorm(x[r]) as cbq_rmsnorm.  *epoch_dev counts the steps (the
+ * caller increments it once per step before the first producer). */
+int cbq_rmsnorm_allreduce(void *x_dev, const void *slots_dev, const uint32_t *counts_dev,
+                          const uint32_t *epoch_dev, int64_t expect, int world, int dtype, int64_t rows,
+                          int64_t n, const float *weight_dev, float eps, void *out_dev,
+                          uint32_t *status_dev, void *stream);
 
 /* The attention block's element-wise part for the token at position *pos_dev
  * (device int64): per-head RMSNorm of q [B, Hq*d] and k [B, Hkv*d] (weights

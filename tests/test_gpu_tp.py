@@ -1,7 +1,9 @@
-"""Tensor-parallel decode on two GPUs (NCCL): the greedy tokens of a TP=2
-model equal those of the same model on one GPU (fp32 activations; only the
-summation order of the all-reduced partial products differs).  Skipped on
-machines with fewer than two GPUs."""
+"""Tensor-parallel decode on two GPUs: the greedy tokens of a TP=2 model equal
+those of the same model on one GPU (fp32 activations; only the summation order
+of the all-reduced partial products differs), with the row-parallel layers'
+all-reduce done by the fused peer-memory path (GEMV epilogue writes into every
+rank's slot, the RMSNorm kernel sums) or by NCCL.  Skipped on machines with
+fewer than two GPUs."""
 import os
 import socket
 import sys
@@ -28,7 +30,7 @@ def _prompt():
     return torch.randint(0, CFG.vocab, (2, 12), generator=torch.Generator().manual_seed(8))
 
 
-def _rank_main(rank, world, port, fused, huffman, q):
+def _rank_main(rank, world, port, fused, huffman, q, allreduce="peer"):
     try:
         sys.path[:0] = [str(REPO), str(REPO / "tests")]
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -43,23 +45,29 @@ def _rank_main(rank, world, port, fused, huffman, q):
                                 timeout=timedelta(seconds=60))
         W = pkg.qwen3.CompressedQwen3Weights(CFG, dev, huffman=huffman, rank=rank, world=world, seed=3)
         dec = qd.Qwen3Decoder(W, batch=2, max_len=40, act_dtype=torch.float32, group=dist.group.WORLD,
-                              fused=fused)
+                              fused=fused, allreduce=allreduce)
+        peer = dec.peer is not None
         eager = dec.generate(_prompt(), 12).cpu()
         dec.reset()
         dec.capture()
         dec.reset()
         graphed = dec.generate(_prompt(), 12).cpu()
         dec.release()
+        if peer and int(dec.peer.status[0].item()) != 0:
+            raise RuntimeError(f"peer all-reduce reported status {dec.peer.status.tolist()}")
+        del dec
         dist.barrier()
         dist.destroy_process_group()
-        q.put((rank, "ok", eager.tolist(), graphed.tolist()))
+        q.put((rank, "ok" if (peer or allreduce != "peer" or not fused or huffman) else "peer path not used",
+               eager.tolist(), graphed.tolist()))
     except BaseException as e:
         q.put((rank, f"{type(e).__name__}: {e}", None, None))
 
 
-@pytest.mark.parametrize("fused", [True, False], ids=["fused", "torch-ops"])
+@pytest.mark.parametrize("fused,allreduce", [(True, "peer"), (True, "nccl"), (False, "nccl")],
+                         ids=["fused-peer", "fused-nccl", "torch-ops"])
 @pytest.mark.parametrize("huffman", [False, True], ids=["fixed", "huffman"])
-def test_tp2_decode_matches_one_gpu(fused, huffman):
+def test_tp2_decode_matches_one_gpu(fused, allreduce, huffman):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import importlib
@@ -71,7 +79,7 @@ def test_tp2_decode_matches_one_gpu(fused, huffman):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, fused, huffman, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, fused, huffman, q, allreduce)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
