@@ -45,6 +45,7 @@ SIGNATURES = {
     "cbq_huff_tables_max_len": (_INT, [_P]),
     "cbq_huff_stream_bytes": (_I64, [_I64]),
     "cbq_huff_chunk_count": (_I64, [_I64, _I64]),
+    "cbq_huff_chunk_table_words": (_I64, [_I64, _I64]),
     "cbq_huff_chunk_table": (_INT, [_P, _I64, _P, _P, _I64, _I64, _I64, _P, _P, _P]),
     "cbq_huff_decode_lut_bytes": (_I64, []),
     "cbq_huff_build_decode_lut": (_INT, [_P, _P, _I64, _P, _P]),

@@ -17,12 +17,15 @@
 //   * the decode tables and the first units are loaded before the
 //     programmatic-dependent-launch wait, i.e. while the previous kernel on
 //     the stream finishes.
-// A symbol costs one shared load from the 14-bit first level, plus a second
-// one taken by the lanes together only when one of them has a longer code;
-// bit patterns that match no code decode through guard entries as the
-// reference does (symbol 0, one bit), and the canonical search remains for
-// prefixes whose second level did not fit.  A partial last chunk of a row
-// (K % 64 != 0) is decoded symbol by symbol.
+// With a value-mode table whose two levels resolve every prefix (lossless
+// codebooks), a lane runs four branch-free decoders over its chunk, from its
+// codes 0, 16, 32 and 48 (the load-time quarter lengths): a
+// symbol costs one shared load from the 14-bit first level and a predicated
+// one from the second level.  Bit patterns that match no code decode through
+// guard entries as the reference does (symbol 0, one bit).  Other tables
+// (symbol payloads, prefixes left to the canonical search) take a
+// one-decoder loop whose second-level load is voted per symbol; a partial
+// last chunk of a row (K % 64 != 0) is decoded symbol by symbol.
 #pragma once
 #include "cbq_huff_kernel.cuh"
 
@@ -55,6 +58,10 @@ struct HgArgs {
     int out_bf16;
     uint32_t cap;                     // bytes per ring slot
     uint32_t *status;
+    // 4 and 1 << 16 as kernel arguments: the scalings written as products in
+    // the decoders stay multiply(-high)-adds on the FMA pipe instead of shifts
+    // and masks on the integer pipe, which the decode saturates
+    uint32_t m4, m16;
 };
 
 __host__ __device__ inline size_t hg_part_bytes(int rows_per_cta, int nseg) {
@@ -65,39 +72,51 @@ __host__ __device__ inline size_t hg_prefix_bytes(int rows_per_cta, int nseg) {
            a128((size_t)kHfSubMax * 4);
 }
 
-template <int NF>
-__device__ __forceinline__ void hg_load_x(const float *xr, int k0, int n, float (&v)[NF]) {
-    if (n == NF) {
-        const float4 *p = reinterpret_cast<const float4 *>(xr + k0);
+// A lane's 64 activations in registers: fp32, or for bf16 inputs the bf16
+// pairs as loaded (32 registers; element i is widened where it is used, one
+// shift or mask), which leaves the decoders room to overlap.
+template <typename XT> struct HgX;
+template <> struct HgX<float> {
+    float v[kHgNF];
+    __device__ __forceinline__ float operator[](int i) const { return v[i]; }
+    __device__ __forceinline__ void load(const float *xr, int k0, int n) {
+        if (n == kHgNF) {
+            const float4 *p = reinterpret_cast<const float4 *>(xr + k0);
 #pragma unroll
-        for (int q = 0; q < NF / 4; ++q) {
-            const float4 f = __ldg(p + q);
-            v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
+            for (int q = 0; q < kHgNF / 4; ++q) {
+                const float4 f = __ldg(p + q);
+                v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < kHgNF; ++i) v[i] = i < n ? __ldg(xr + k0 + i) : 0.f;
         }
-    } else {
-#pragma unroll
-        for (int i = 0; i < NF; ++i) v[i] = i < n ? __ldg(xr + k0 + i) : 0.f;
     }
-}
-template <int NF>
-__device__ __forceinline__ void hg_load_x(const __nv_bfloat16 *xr, int k0, int n, float (&v)[NF]) {
-    if (n == NF) {
-        const uint4 *p = reinterpret_cast<const uint4 *>(xr + k0);
+};
+template <> struct HgX<__nv_bfloat16> {
+    uint32_t v[kHgNF / 2];
+    __device__ __forceinline__ float operator[](int i) const {
+        return __uint_as_float((i & 1) ? (v[i >> 1] & 0xffff0000u) : (v[i >> 1] << 16));
+    }
+    __device__ __forceinline__ void load(const __nv_bfloat16 *xr, int k0, int n) {
+        if (n == kHgNF) {
+            const uint4 *p = reinterpret_cast<const uint4 *>(xr + k0);
 #pragma unroll
-        for (int q = 0; q < NF / 8; ++q) {
-            const uint4 f = __ldg(p + q);
-            const uint32_t u[4] = {f.x, f.y, f.z, f.w};
+            for (int q = 0; q < kHgNF / 8; ++q) {
+                const uint4 f = __ldg(p + q);
+                v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
+            }
+        } else {
+            const uint16_t *h = reinterpret_cast<const uint16_t *>(xr + k0);
 #pragma unroll
-            for (int h = 0; h < 4; ++h) {
-                v[8 * q + 2 * h] = __uint_as_float(u[h] << 16);
-                v[8 * q + 2 * h + 1] = __uint_as_float(u[h] & 0xffff0000u);
+            for (int i = 0; i < kHgNF / 2; ++i) {
+                const uint32_t lo = 2 * i < n ? (uint32_t)__ldg(h + 2 * i) : 0u;
+                const uint32_t hi = 2 * i + 1 < n ? (uint32_t)__ldg(h + 2 * i + 1) : 0u;
+                v[i] = lo | (hi << 16);
             }
         }
-    } else {
-#pragma unroll
-        for (int i = 0; i < NF; ++i) v[i] = i < n ? __bfloat162float(xr[k0 + i]) : 0.f;
     }
-}
+};
 
 __device__ __forceinline__ uint32_t hg_lds(uint32_t addr) {
     uint32_t v;
@@ -154,8 +173,8 @@ struct HgBits {
 // a full chunk) take the second-level load together, predicated, only when
 // one of them needs it.  CANON (a table whose second level did not fit for
 // some prefixes): such a prefix's entry is 0 and takes the canonical search.
-template <bool VALUE, bool RING, bool CANON>
-__device__ __forceinline__ float hg_chunk_fast(HgBits<RING> &bb, const float (&xr)[kHgNF], uint32_t mask,
+template <bool VALUE, bool RING, bool CANON, typename XV>
+__device__ __forceinline__ float hg_chunk_fast(HgBits<RING> &bb, const XV &xr, uint32_t mask,
                                                uint32_t lut_s, uint32_t sub_s, const HuffSlow *hs,
                                                const uint16_t *gsyms, const float *gcb, uint32_t cmax) {
     float acc0 = 0.f, acc1 = 0.f;
@@ -186,10 +205,102 @@ __device__ __forceinline__ float hg_chunk_fast(HgBits<RING> &bb, const float (&x
     return acc0 + acc1;
 }
 
+// ld.shared taken only when p is set; otherwise v keeps its value.
+__device__ __forceinline__ uint32_t hg_lds_if(uint32_t p, uint32_t addr, uint32_t v) {
+    asm("{\n\t.reg .pred q;\n\tsetp.ne.u32 q, %2, 0;\n\t@q ld.shared.u32 %0, [%1];\n\t}"
+        : "+r"(v) : "r"(addr), "r"(p));
+    return v;
+}
+
+// One decoder of the fast path: a window of two byte-swapped stream words
+// hi:lo, the raw word after them (nx), the shared address of the word after
+// nx (wa) and a running bit count `pos` whose low five bits are the offset of
+// the next code in hi (the funnel shift wraps).
+struct HgDec {
+    uint32_t hi, lo, nx, wa, pos;
+    __device__ __forceinline__ void init(uint32_t addr, uint32_t bit) {   // addr: slot's word 0
+        const uint32_t a0 = addr + ((bit >> 5) << 2);
+        hi = bswap32(hg_lds(a0));
+        lo = bswap32(hg_lds(a0 + 4u));
+        nx = hg_lds(a0 + 8u);
+        wa = a0 + 12u;
+        pos = bit & 31u;
+    }
+    // One code in three phases, so that a lane's decoders can be interleaved
+    // phase by phase (a warp issues in order: the loads of all decoders go
+    // out before any of their results is needed).  Value-mode two-level table:
+    //   * the first-level entry of a pointer prefix holds the second-level
+    //     offset (bits 31:16) and 32 - depth (bits 4:0, which the wrapping
+    //     funnel shift uses as its count); the second-level load is
+    //     predicated on bit 7, so there is no branch;
+    //   * an entry's low 16 bits are its code length: the weight is the entry
+    //     with them cleared and the position advances by the length;
+    //   * a code crossed into lo exactly when bit 5 of `pos` flipped; the
+    //     window then moves one word and only those lanes load the word after
+    //     it (needed at their next crossing at the earliest), one predicate
+    //     for the four moves.
+    uint32_t win, e;
+    __device__ __forceinline__ void look(uint32_t lut_s, uint32_t m4) {
+        win = __funnelshift_l(lo, hi, pos);
+        e = hg_lds((win >> (32 - kHfLutBits)) * m4 + lut_s);
+    }
+    __device__ __forceinline__ void resolve(uint32_t sub_s, uint32_t m4, uint32_t m16) {
+        const uint32_t a2 = (__umulhi(e, m16) + __funnelshift_r(win << kHfLutBits, 0u, e)) * m4 + sub_s;
+        asm("{\n\t.reg .pred q;\n\t.reg .b32 t;\n\t"
+            "and.b32 t, %0, 128;\n\tsetp.ne.u32 q, t, 0;\n\t"
+            "@q ld.shared.u32 %0, [%1];\n\t}" : "+r"(e) : "r"(a2));
+    }
+    __device__ __forceinline__ float consume(float x, float acc) {
+        const uint32_t wt = e & 0xffff0000u;
+        const uint32_t len = e - wt;
+        const uint32_t np = pos + len;
+        asm("{\n\t.reg .pred q;\n\t.reg .b32 t;\n\t"
+            "xor.b32 t, %4, %5;\n\tand.b32 t, t, 32;\n\tsetp.ne.u32 q, t, 0;\n\t"
+            "@q mov.b32 %0, %1;\n\t"
+            "@q prmt.b32 %1, %2, 0, 0x0123;\n\t"
+            "@q ld.shared.u32 %2, [%3];\n\t"
+            "@q add.u32 %3, %3, 4;\n\t}"
+            : "+r"(hi), "+r"(lo), "+r"(nx), "+r"(wa) : "r"(np), "r"(pos));
+        pos = np;
+        return fmaf(x, __uint_as_float(wt), acc);
+    }
+};
+
+// The common case: a value-mode table with every prefix resolved by its two
+// levels, and the chunk in the ring.  Four independent decoders per lane,
+// from the chunk's codes 0, 16, 32 and 48 (the packed quarter lengths of the
+// load-time table), interleaved phase by phase against the same registers of
+// x: straight-line code whose four dependency chains (window, first- and
+// second-level loads) overlap.  The ring slot holds the unit plus 32 bytes,
+// so every word a decoder reads is inside the slot.
+template <typename XV>
+__device__ __forceinline__ float hg_chunk_v2(uint32_t ws, uint32_t bit0, uint32_t quarters, const XV &xr,
+                                             uint32_t lut_s, uint32_t sub_s, uint32_t m4, uint32_t m16) {
+    constexpr int kQ = kHgNF / 4;
+    HgDec d[4];
+    uint32_t b = bit0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        d[j].init(ws, b);
+        b += (quarters >> (10 * j)) & 1023u;
+    }
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int q = 0; q < kQ; ++q) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) d[j].look(lut_s, m4);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) d[j].resolve(sub_s, m4, m16);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[j] = d[j].consume(xr[j * kQ + q], acc[j]);
+    }
+    return (acc[0] + acc[1]) + (acc[2] + acc[3]);
+}
+
 // Any chunk with any table (a partial last chunk, or a two-level table that
 // left prefixes to the canonical search): symbol by symbol.
-template <bool VALUE>
-__device__ __forceinline__ float hg_chunk_any(Bits32 &bb, const float (&xr)[kHgNF], int nsym, const uint32_t *lut,
+template <bool VALUE, typename XV>
+__device__ __forceinline__ float hg_chunk_any(Bits32 &bb, const XV &xr, int nsym, const uint32_t *lut,
                                               const uint32_t *sub, const HuffSlow *hs, const uint16_t *gsyms,
                                               const float *gcb, uint32_t cmax, uint32_t &bad) {
     float acc = 0.f;
@@ -230,6 +341,12 @@ __device__ __forceinline__ void hg_loop(const HgArgs &a, const uint32_t *lut, co
         const int q = 32 * s + lane;
         return (q < nch) ? a.rbs[r] + (int64_t)a.chunk[r * nch + q] : -1;
     };
+    // packed bit lengths of the quarters of this lane's chunk (fast path decoders)
+    const uint32_t *quarter = a.chunk + (int64_t)a.M * nch;
+    auto lane_quarters = [&](int64_t r, int s) -> uint32_t {
+        const int q = 32 * s + lane;
+        return (VALUE && !CANON && q < nch) ? quarter[r * nch + q] : 0u;
+    };
     auto unit_end = [&](int64_t r, int s) -> int64_t {
         if (32 * s + 32 < nch) return a.rbs[r] + (int64_t)a.chunk[r * nch + 32 * s + 32];
         return (r + 1 < a.M) ? a.rbs[r + 1] : a.total_bits;
@@ -250,10 +367,12 @@ __device__ __forceinline__ void hg_loop(const HgArgs &a, const uint32_t *lut, co
     int ps = u0 / nrows, prl = u0 - (u0 / nrows) * nrows;
     static_assert(kHgSlots == 2, "the start bits below are kept for two slots");
     int64_t st0 = -1, st1 = -1;                            // this lane's start bit, per slot
+    uint32_t hf0 = 0, hf1 = 0;                             // and its chunk's quarter lengths
     for (int i = 0; i < n && i < kHgSlots; ++i) {
         const int64_t r = m0 + prl;
         const int64_t sb = lane_start(r, ps);
-        if (i == 0) st0 = sb; else st1 = sb;
+        const uint32_t hf = lane_quarters(r, ps);
+        if (i == 0) { st0 = sb; hf0 = hf; } else { st1 = sb; hf1 = hf; }
         const int64_t eb = (lane == 0) ? unit_end(r, ps) : 0;
         if (lane == 0) issue(i, sb, eb);
         if (++prl == nrows) { prl = 0; ++ps; }
@@ -261,7 +380,7 @@ __device__ __forceinline__ void hg_loop(const HgArgs &a, const uint32_t *lut, co
     __syncwarp();
     pdl_wait();                                            // activations come from the previous kernel
 
-    float xr[kHgNF];
+    HgX<XT> xr;
     int xs = -1;
     int s = u0 / nrows, rl = u0 - (u0 / nrows) * nrows;
     int slot = 0;
@@ -271,15 +390,18 @@ __device__ __forceinline__ void hg_loop(const HgArgs &a, const uint32_t *lut, co
         const int q = 32 * s + lane;                       // this lane's chunk
         const int nsym = q < nch ? min(kHgNF, K - q * kHgNF) : 0;
         if (s != xs) {
-            if (nsym > 0) hg_load_x<kHgNF>(x, q * kHgNF, nsym, xr);
+            if (nsym > 0) xr.load(x, q * kHgNF, nsym);
             xs = s;
         }
         const int64_t my_bit = slot ? st1 : st0;
+        const uint32_t my_quarters = slot ? hf1 : hf0;
         int64_t nx_sb = -1, nx_eb = 0;
+        uint32_t nx_hf = 0;
         const bool more = i + kHgSlots < n;
         if (more) {                                        // offsets of the unit that reuses this slot
             const int64_t r2 = m0 + prl;
             nx_sb = lane_start(r2, ps);
+            nx_hf = lane_quarters(r2, ps);
             if (lane == 0) nx_eb = unit_end(r2, ps);
             if (++prl == nrows) { prl = 0; ++ps; }
         }
@@ -301,7 +423,10 @@ __device__ __forceinline__ void hg_loop(const HgArgs &a, const uint32_t *lut, co
                                             : reinterpret_cast<const uint32_t *>(a.stream);
             const uint32_t nw = b0 >= 0 ? a.cap / 4 : (uint32_t)min((int64_t)0xffffffff, a.stream_bytes / 4);
             const uint64_t pos = b0 >= 0 ? (uint64_t)(my_bit - 8 * b0) : (uint64_t)my_bit;
-            if (nsym == kHgNF && b0 >= 0) {
+            if (VALUE && !CANON && nsym == kHgNF && b0 >= 0) {
+                acc = hg_chunk_v2(smem_u32(wbase), (uint32_t)pos, my_quarters, xr, smem_u32(lut), smem_u32(sub),
+                                  a.m4, a.m16);
+            } else if (nsym == kHgNF && b0 >= 0) {
                 HgBits<true> bb;
                 bb.init(wbase, nw, pos);
                 acc = hg_chunk_fast<VALUE, true, CANON>(bb, xr, fast_ring, smem_u32(lut), smem_u32(sub), hs,
@@ -320,7 +445,7 @@ __device__ __forceinline__ void hg_loop(const HgArgs &a, const uint32_t *lut, co
         if (bad) report(a.status, CBQ_FLAG_CORRUPT, (uint32_t)(m0 + rl));
         __syncwarp();
         if (more) {
-            if (slot) st1 = nx_sb; else st0 = nx_sb;
+            if (slot) { st1 = nx_sb; hf1 = nx_hf; } else { st0 = nx_sb; hf0 = nx_hf; }
             if (lane == 0) issue(slot, nx_sb, nx_eb);
         }
         const float tot = warp_sum(acc);

@@ -96,14 +96,22 @@ __global__ void __launch_bounds__(128) k_huff_chunks(const uint8_t *stream, uint
     const int64_t start = rbs[r];
     BitBuf bb;
     bb.init(reinterpret_cast<const uint32_t *>(stream), nwords, (uint64_t)start);
-    int64_t pos = start;
-    uint32_t bad = 0;
+    int64_t pos = start, q0 = start;
+    uint32_t bad = 0, quarters = 0;
     bool overflow = false;
+    uint32_t *quarter = chunk + M * nch;
+    static_assert(S == 64, "three 10-bit quarter lengths per 64-symbol chunk");
     for (int64_t k = 0; k < K; ++k) {
         if ((k % S) == 0) {
             const int64_t rel = pos - start;
             overflow |= rel > 0xffffffffll;
             chunk[r * nch + k / S] = (uint32_t)rel;
+            if (k) quarter[r * nch + k / S - 1] = quarters;
+            quarters = 0;
+            q0 = pos;
+        } else if ((k % 16) == 0) {                               // at most 16 codes of at most 32 bits
+            quarters |= (uint32_t)(pos - q0) << (10 * (int)((k % S) / 16 - 1));
+            q0 = pos;
         }
         int len;
         decode_sym(bb.buf, &st, gsyms, len);
@@ -111,6 +119,7 @@ __global__ void __launch_bounds__(128) k_huff_chunks(const uint8_t *stream, uint
         bb.consume(len);
         pos += len;
     }
+    if (K) quarter[r * nch + nch - 1] = quarters;
     if (bad) report(status, CBQ_FLAG_CORRUPT, (uint32_t)r);
     const bool last = (r + 1 == M);
     const bool end_ok = last ? (pos <= total_bits && pos > total_bits - 8) || (K == 0)
@@ -160,7 +169,7 @@ __global__ void __launch_bounds__(1024) k_huff_build_lut(const HuffTables *tab, 
             lut[p] = (payload(sym) << 16) | (uint32_t)L0;
         } else if (L0 == 0 && code_len_at(tab, (p << (32 - kHfLutBits)) | ((1u << (32 - kHfLutBits)) - 1u),
                                           sym) == 0) {
-            lut[p] = (payload(0) << 16) | 0x40u | 1u;           // no code starts here: guard
+            lut[p] = (payload(0) << 16) | 1u;           // no code starts here: guard
         } else if (L0 > kHfLutBits || L0 == 0) {
             uint32_t s2;
             int L1 = code_len_at(tab, (p << (32 - kHfLutBits)) | ((1u << (32 - kHfLutBits)) - 1u), s2);
@@ -206,7 +215,7 @@ __global__ void __launch_bounds__(1024) k_huff_build_lut(const HuffTables *tab, 
                 uint32_t sym;
                 const int L = code_len_at(tab, w, sym);
                 sub[off + k] = (L > kHfLutBits) ? ((payload(sym) << 16) | (uint32_t)L)
-                                                : ((payload(0) << 16) | 0x40u | 1u);
+                                                : ((payload(0) << 16) | 1u);
             }
             used_max = max(used_max, off + n);
         } else {
@@ -488,6 +497,11 @@ extern "C" int64_t cbq_huff_chunk_count(int64_t M, int64_t K) {
     return M * ((K + S - 1) / S);
 }
 
+extern "C" int64_t cbq_huff_chunk_table_words(int64_t M, int64_t K) {
+    const int64_t n = cbq_huff_chunk_count(M, K);
+    return n < 0 ? -1 : 2 * n;
+}
+
 extern "C" int cbq_huff_chunk_table(const uint8_t *stream_dev, int64_t stream_bytes,
                                     const void *tables_dev, const int64_t *rbs_dev, int64_t M,
                                     int64_t K, int64_t total_bits, uint32_t *chunk_dev,
@@ -554,6 +568,7 @@ extern "C" int cbq_linear_huff(const void *x_dev, int x_dtype, int64_t T, int64_
         h.M = (int)M; h.K = (int)K; h.nch = (int)((K + S - 1) / S); h.nseg = g.nseg;
         h.rows_per_cta = g.rows_per_cta; h.bias = bias_dev; h.out = out_dev; h.ldo = ldo;
         h.out_bf16 = out_dtype == CBQ_BF16; h.cap = g.cap; h.status = status_dev;
+        h.m4 = 4u; h.m16 = 1u << 16;
         return x_dtype == CBQ_BF16 ? launch_hgemv<__nv_bfloat16>(h, g, s) : launch_hgemv<float>(h, g, s);
     }
     HuffPlan p;

@@ -59,8 +59,9 @@ __host__ __device__ inline const uint16_t *blob_syms(const HuffTables *t) {
 // The decode table (device buffer built by cbq_huff_build_decode_lut):
 //   words [0, 16384): first level, indexed by the next 14 bits.
 //     (payload << 16) | len for a code of length 1..14;
-//     (payload(0) << 16) | 0x40 | 1 where no code starts with the prefix (an
+//     (payload(0) << 16) | 1 where no code starts with the prefix (an
 //       incomplete code): the reference's guard, symbol 0 consuming one bit;
+//     (so the low 16 bits of every resolved entry are exactly its length);
 //     (offset << 16) | 0x80 | (32 - depth) for a prefix of longer codes: the
 //       code's entry is second-level word offset + (the depth bits after the
 //       prefix), i.e. sub[offset + ((window << 14) >> (32 - depth))];

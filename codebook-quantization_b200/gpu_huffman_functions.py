@@ -94,7 +94,8 @@ class HuffmanStream:
         if self.rbs.numel() != self.rows:
             raise ValueError(f"{name}: {self.rbs.numel()} row bit starts for {self.rows} rows")
         self.nchunk = _lib.query("cbq_huff_chunk_count", self.rows, self.cols)
-        self.chunk = torch.zeros(max(self.nchunk, 1), dtype=torch.int32, device=device)
+        words = _lib.query("cbq_huff_chunk_table_words", self.rows, self.cols)
+        self.chunk = torch.zeros(max(words, 1), dtype=torch.int32, device=device)
         self.status = new_status(device)
         _lib.call("cbq_huff_chunk_table", self.stream.data_ptr(), self.nbytes, self.tables.data_ptr(),
                   self.rbs.data_ptr(), self.rows, self.cols, self.total_bits, self.chunk.data_ptr(),
@@ -121,8 +122,9 @@ class HuffmanStream:
 
     @property
     def compressed_bytes(self) -> int:
-        """Algorithmic bytes one full pass reads: stream + row starts + chunk table."""
-        return self.stream_len + 8 * self.rows + 4 * self.nchunk
+        """Algorithmic bytes one full pass reads: stream + row starts + chunk
+        table (32-bit chunk offsets and 32-bit packed quarter lengths)."""
+        return self.stream_len + 8 * self.rows + 8 * self.nchunk
 
 
 class HuffmanCodebookLinear:

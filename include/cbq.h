@@ -203,17 +203,26 @@ int cbq_huff_tables_max_len(const void *tables_host);
  * has stream_len bytes (it already ends with 4 zero bytes). */
 int64_t cbq_huff_stream_bytes(int64_t stream_len);
 
-/* Symbols per entry of the chunk-entry table, and its element count. */
+/* Symbols per entry of the chunk-entry table, its entry count
+ * (M * ceil(K/64)), and the 32-bit words to allocate for the table. */
 #define CBQ_HUFF_CHUNK 64
 int64_t cbq_huff_chunk_count(int64_t M, int64_t K);
+int64_t cbq_huff_chunk_table_words(int64_t M, int64_t K);
 
 /* Load-time pass: decode every row once and record, for each row r and
- * chunk c, the bit offset of symbol c*64 relative to row_bit_starts[r]
- * (uint32_t chunk_dev[M * ceil(K/64)]).  The reference format has only
- * per-row entry points (src/huffman_codebook.py:213); this table gives the
- * GEMV 64-symbol entry points.  Records CBQ_FLAG_ROW_END when a row does
- * not end where the next one starts and CBQ_FLAG_CORRUPT for undecodable
- * codes, in status_dev. */
+ * chunk c (n = cbq_huff_chunk_count(M, K) entries, chunk_dev holding
+ * cbq_huff_chunk_table_words(M, K) = 2n words):
+ *   uint32_t chunk_dev[n]: bit offset of symbol c*64 relative to
+ *     row_bit_starts[r];
+ *   uint32_t quarter[n] (at chunk_dev + n): bits 0-9, 10-19 and 20-29 hold
+ *     the bit lengths of the chunk's codes 0-15, 16-31 and 32-47 (each at
+ *     most 16 * 32 = 512; 0 unless the row goes on past the group), so the
+ *     one-token GEMV runs four independent decoders per chunk.
+ * The reference format has only per-row entry points
+ * (src/huffman_codebook.py:213); this table gives the GEMV its 64- and
+ * 16-symbol entry points.  Records CBQ_FLAG_ROW_END when a row does not end
+ * where the next one starts and CBQ_FLAG_CORRUPT for undecodable codes, in
+ * status_dev. */
 int cbq_huff_chunk_table(const uint8_t *stream_dev, int64_t stream_bytes,
                          const void *tables_dev, const int64_t *row_bit_starts_dev,
                          int64_t M, int64_t K, int64_t total_bits,

@@ -41,6 +41,7 @@ def test_size_queries():
     assert lib.cbq_fixed_stream_bytes(1, 1, 17) == -1
     assert lib.cbq_huff_stream_bytes(100) >= 100 + 16
     assert lib.cbq_huff_chunk_count(10, 130) == 10 * 3
+    assert lib.cbq_huff_chunk_table_words(10, 130) == 2 * 30       # offsets + packed quarter lengths
     assert lib.cbq_huff_tables_bytes(0) == -1
 
 

@@ -48,8 +48,18 @@ def test_chunk_table_matches_oracle(case):
     d = golden(f"huff_{case}.npz")
     M, K = (int(v) for v in d["shape"])
     hs = stream_of(d, dev)
-    got = hs.chunk.cpu().numpy().view(np.uint32)[:hs.nchunk].astype(np.int64)
+    raw = hs.chunk.cpu().numpy()
+    got = raw.view(np.uint32)[:hs.nchunk].astype(np.int64)
     np.testing.assert_array_equal(got, oracle.huff_chunk_offsets(d, M, K, 64))
+    # quarter lengths: bits 10j..10j+9 = bit length of codes 16j..16j+15 of the
+    # chunk (j = 0, 1, 2), 0 unless code 16j+16 is in the row
+    qw = raw.view(np.uint32)[hs.nchunk:2 * hs.nchunk].astype(np.int64).reshape(M, -1)
+    o16 = oracle.huff_chunk_offsets(d, M, K, 16).reshape(M, -1)
+    for c in range(qw.shape[1]):
+        for j in range(3):
+            k0, k1 = 64 * c + 16 * j, 64 * c + 16 * (j + 1)
+            want = o16[:, k1 // 16] - o16[:, k0 // 16] if k1 < K else np.zeros(M, np.int64)
+            np.testing.assert_array_equal((qw[:, c] >> (10 * j)) & 1023, want, err_msg=f"chunk {c} quarter {j}")
 
 
 @pytest.mark.parametrize("case", CASES)
@@ -65,6 +75,25 @@ def test_linear_huff_matches_oracle(case, T):
     y = lin(torch.from_numpy(x).to(dev)).cpu().numpy()
     ref = oracle.huff_linear(x, d, cb, M, K)
     assert rel_l2(y, ref) < 1e-5
+    lin.hs.check()
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_linear_huff_value_mode_matches_oracle(case):
+    """bf16-exact codebook values: the decode table carries the weights
+    themselves, which the one-token kernel decodes with four branch-free decoders
+    per chunk (guards, second-level codes and 32-bit codes included)."""
+    dev = need_cuda()
+    d = golden(f"huff_{case}.npz")
+    M, K = (int(v) for v in d["shape"])
+    cb = torch.from_numpy(codebook_for(d, 2)).to(torch.bfloat16).float().numpy()
+    lin = HS.HuffmanCodebookLinear("v", d["huff_stream"], d["huff_lengths"], int(d["huff_n"][0]), cb,
+                                   (M, K), 13, huff_row_bit_starts=d["huff_row_bit_starts"], device=dev)
+    for T, xdt in ((1, torch.float32), (1, torch.bfloat16), (2, torch.float32)):
+        x = torch.from_numpy(np.random.default_rng(T).standard_normal((T, K)).astype(np.float32)).to(xdt)
+        y = lin(x.to(dev)).float().cpu().numpy()
+        ref = oracle.huff_linear(x.float().numpy(), d, cb, M, K)
+        assert rel_l2(y, ref) < (1e-5 if xdt == torch.float32 else 5e-3), (T, xdt)
     lin.hs.check()
 
 
