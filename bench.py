@@ -61,6 +61,24 @@ def parse():
     return ap.parse_args()
 
 
+# DRAM bytes (read + write) per launch of the dominant kernel, measured once
+# with ncu on the same shape (profiles/<kernel>_gemv_12288x4096_t1.md); the
+# roofline's `traffic`.  Keyed by (kernel, M, K, tokens).
+NCU_TRAFFIC = {
+    ("k_gemv_fixed", 12288, 4096, 1): 81.880832e6 + 2.562048e6,
+    ("k_gemv_huff", 12288, 4096, 1): 72.563456e6 + 1.255424e6,
+}
+
+
+def gemv_kernel_name(huffman: bool, tokens: int, x_bf16: bool = True) -> str:
+    """The kernel cbq_linear_fixed / cbq_linear_huff dispatch to for `tokens` rows."""
+    if huffman:
+        return "k_gemv_huff" if tokens == 1 else "k_linear_huff"
+    if tokens <= 2:
+        return "k_gemv_fixed"
+    return "k_gemm_fixed" if tokens >= 64 and x_bf16 else "k_linear_fixed"
+
+
 def measured_peaks():
     p = REPO / "MEASURED_PEAKS.json"
     if p.exists():
@@ -250,7 +268,7 @@ def gemv_workload(args):
     us = ms * 1e3 / R
     gbs = alg / R / (us * 1e-6) / 1e9
     peak, peak_kind = measured_peaks()
-    kern = "k_linear_huff" if args.huffman else "k_linear_fixed"
+    kern = gemv_kernel_name(args.huffman, T, args.x_dtype == "bf16")
     line = {"metric": "compressed GEMV GB/s vs HBM", "value": gbs, "unit": "GB/s", "n_gpus": 1,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": args.x_dtype,
@@ -259,7 +277,8 @@ def gemv_workload(args):
                        "copies": R, "l2": f"{R} distinct matrices rotated (> 2x L2)",
                        "bits": mats[0].bits},
             "roofline": {"kernel": kern, "bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
-                         "frac": gbs / peak, "peak_kind": peak_kind, "traffic": None,
+                         "frac": gbs / peak, "peak_kind": peak_kind,
+                         "traffic": NCU_TRAFFIC.get((kern, M, K, T)),
                          "alg_bytes_per_launch": alg / R, "us_per_launch": us},
             "gpu_launches": args.steps * R, "clocks": clk.summary()}
     print(json.dumps(line), flush=True)
@@ -438,10 +457,11 @@ def main():
                        "stream_bytes_per_rank": stack_bytes,
                        "hbm_gbs_whole_step": stack_bytes / (ms_step * 1e-3) / 1e9,
                        "setup_s": round(setup_s, 1)},
-            "roofline": {"kernel": ("k_linear_huff" if args.huffman else "k_linear_fixed<13,1,bf16,bf16>")
-                                   + f" gate_proj {g0.M}x{g0.K}",
+            "roofline": {"kernel": gemv_kernel_name(args.huffman, args.batch) + f" gate_proj {g0.M}x{g0.K}",
                          "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
+                         "frac": achieved / peak, "peak_kind": peak_kind,
+                         "traffic": NCU_TRAFFIC.get((gemv_kernel_name(args.huffman, args.batch), g0.M, g0.K,
+                                                     args.batch)),
                          "alg_bytes_per_launch": alg, "us_per_launch": gms * 1e3,
                          "timing": "CUDA-graph replay of the 36 gate_proj launches, CUDA events"},
             "e2e": {"value": args.batch * 1000.0 / ms_e2e, "unit": "tok/s",
