@@ -56,6 +56,10 @@ def parse():
     ap.add_argument("--shape", default="12288,4096", help="gemv workload: M,K")
     ap.add_argument("--tokens", type=int, default=1, help="gemv workload: T (activation rows)")
     ap.add_argument("--x-dtype", default="bf16", choices=["bf16", "f32"], help="gemv workload: activation dtype")
+    ap.add_argument("--fuse-norm", action="store_true",
+                    help="decode: RMSNorm in the last CTA of the GEMV before it instead of its own launch")
+    ap.add_argument("--split-rope", action="store_true",
+                    help="decode: q/k norm + rope as its own launch instead of in the attention launch")
     ap.add_argument("--allreduce", default="peer", choices=["peer", "nccl"],
                     help="tensor parallelism: fused peer-memory all-reduce or NCCL")
     return ap.parse_args()
@@ -364,7 +368,7 @@ def main():
     prompt_len = 64
     max_len = prompt_len + args.warmup + 2 * args.steps + 8
     dec = qd.Qwen3Decoder(W, batch=args.batch, max_len=max_len, act_dtype=torch.bfloat16, group=group,
-                          allreduce=args.allreduce)
+                          allreduce=args.allreduce, fuse_norm=args.fuse_norm, fuse_rope=not args.split_rope)
     g = torch.Generator().manual_seed(1234)
     prompt = torch.randint(0, cfg.vocab, (args.batch, prompt_len), generator=g)
     if not args.no_graph:
@@ -453,6 +457,9 @@ def main():
                        "global_batch": args.batch, "seq_len": max_len, "parallelism": f"tp{world}",
                        "allreduce": ("peer-memory (GEMV epilogue + RMSNorm)" if dec.peer is not None
                                      else ("nccl" if world > 1 else "none")),
+                       "launches_per_layer": ("q/k/v, attention" + ("" if dec.fuse_rope else " (+ q/k norm rope)")
+                                              + ", o" + (" + norm" if dec.fuse_norm else ", norm")
+                                              + ", gate/up, down" + (" + norm" if dec.fuse_norm else ", norm")),
                        "l2": "weights 12.3 GB >> 126 MB L2 (no flush)",
                        "stream_bytes_per_rank": stack_bytes,
                        "hbm_gbs_whole_step": stack_bytes / (ms_step * 1e-3) / 1e9,

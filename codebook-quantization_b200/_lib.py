@@ -36,6 +36,11 @@ SIGNATURES = {
                                       _P, _P, _P, _INT, _INT, _P]),
     "cbq_linear_fixed_peer": (_INT, [_P, _INT, _I64, _I64, _P, _I64, _P, _I64, _INT, _I64, _I64, _P, _INT,
                                      _P, _P, _I64, _INT, _P]),
+    "cbq_linear_fixed_peer_norm": (_INT, [_P, _INT, _I64, _I64, _P, _I64, _P, _I64, _INT, _I64, _I64, _P, _INT,
+                                          _P, _P, _I64, _INT, _P, _P, _P, _I64, _P, _I64, _P, ct.c_float, _P,
+                                          _I64, _P, _P, _P]),
+    "cbq_linear_fixed_residual_norm": (_INT, [_P, _INT, _I64, _I64, _P, _I64, _P, _I64, _INT, _I64, _I64, _P,
+                                              _P, _I64, _INT, _P, ct.c_float, _P, _I64, _P, _P]),
     "cbq_linear_fixed_noalloc": (_INT, [_P, _INT, _I64, _I64, _P, _I64, _P, _I64, _INT, _I64, _I64, _P,
                                         _P, _INT, _I64, _P]),
     "cbq_embedding_fixed": (_INT, [_P, _I64, _P, _I64, _P, _I64, _INT, _I64, _I64, _P, _INT, _P, _P]),
@@ -62,6 +67,8 @@ SIGNATURES = {
     "cbq_qk_norm_rope": (_INT, [_P, _P, _P, _INT, _I64, _I64, _I64, _I64, ct.c_float, _P, _P, _P, _P, _P,
                                 _P, _P, _P, _I64, _P]),
     "cbq_attn_decode": (_INT, [_P, _P, _P, _INT, _I64, _I64, _I64, _I64, _I64, _P, ct.c_float, _P, _P]),
+    "cbq_attn_decode_rope": (_INT, [_P, _P, _P, _INT, _I64, _I64, _I64, _I64, ct.c_float, _P, _P, _P, _P, _P,
+                                    _P, _P, _I64, ct.c_float, _P, _P]),
 }
 CBQ_EPI_STORE, CBQ_EPI_RESIDUAL, CBQ_EPI_SILU_MUL = 0, 1, 2
 

@@ -124,9 +124,48 @@ __global__ void __launch_bounds__(NT) k_rmsnorm_allreduce(T *x, const T *slots, 
 }
 
 // ------------------------------------------- q/k norm + rope + cache write
+// One head held by a warp (lane l: elements [l*E, l*E + E), E = d/32):
+// per-head RMSNorm with weight w (may be null), then rotate_half RoPE with the
+// lane's cos / sin values c, sn of the position; rotate_half's partner of
+// element i is i +- d/2, held by lane l ^ 16.  Rounds to T where the unfused
+// torch sequence does.
+template <typename T, int E>
+__device__ __forceinline__ void qk_head(const float (&x0)[E], float eps, const float *w, const float (&c)[E],
+                                        const float (&sn)[E], int lane, float (&o)[E]) {
+    constexpr int D = 32 * E;
+    float x[E];
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) ss += x0[e] * x0[e];
+    ss = warp_sum(ss);
+    const float scale = rsqrtf(ss / (float)D + eps);
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        x[e] = rnd<T>(x0[e] * scale);
+        if (w) x[e] = rnd<T>(w[lane * E + e] * x[e]);
+    }
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const int i = lane * E + e;
+        const float partner = __shfl_xor_sync(0xffffffffu, x[e], 16);
+        const float rot = i < D / 2 ? -partner : partner;
+        o[e] = rnd<T>(rnd<T>(x[e] * c[e]) + rnd<T>(rot * sn[e]));
+    }
+}
+
+// The lane's cos / sin values of one table row, rounded to T as the torch
+// sequence rounds them.
+template <typename T, int E>
+__device__ __forceinline__ void rope_row(const float *cr, const float *sr, int lane, float (&c)[E], float (&sn)[E]) {
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        c[e] = rnd<T>(cr[lane * E + e]);
+        sn[e] = rnd<T>(sr[lane * E + e]);
+    }
+}
+
 // One warp per head: heads [0, Hq) of q, then Hkv of k, then Hkv of v, for
-// each of B rows.  Lane l holds elements [l*E, l*E + E) with E = d/32;
-// rotate_half's partner of element i is i +- d/2, held by lane l ^ 16.
+// each of B rows.
 template <typename T, int E>
 __global__ void __launch_bounds__(256) k_qk_norm_rope(const T *q, const T *k, const T *v, int B, int Hq,
                                                       int Hkv, float eps, const float *qw, const float *kw,
@@ -157,27 +196,9 @@ __global__ void __launch_bounds__(256) k_qk_norm_rope(const T *q, const T *k, co
         for (int e = 0; e < E; ++e) dst[lane * E + e] = from_f32<T>(x[e]);
         return;
     }
-    float ss = 0.f;
-#pragma unroll
-    for (int e = 0; e < E; ++e) ss += x[e] * x[e];
-    ss = warp_sum(ss);
-    const float scale = rsqrtf(ss / (float)D + eps);
-    const float *wt = kind == 0 ? qw : kw;
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-        x[e] = rnd<T>(x[e] * scale);
-        if (wt) x[e] = rnd<T>(wt[lane * E + e] * x[e]);
-    }
-    const float *cr = cosT + pos * D, *sr = sinT + pos * D;
-    float o[E];
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-        const int i = lane * E + e;
-        const float partner = __shfl_xor_sync(0xffffffffu, x[e], 16);
-        const float rot = i < D / 2 ? -partner : partner;
-        const float c = rnd<T>(cr[i]), s = rnd<T>(sr[i]);
-        o[e] = rnd<T>(rnd<T>(x[e] * c) + rnd<T>(rot * s));
-    }
+    float o[E], c[E], sn[E];
+    rope_row<T, E>(cosT + pos * D, sinT + pos * D, lane, c, sn);
+    qk_head<T, E>(x, eps, kind == 0 ? qw : kw, c, sn, lane, o);
     T *dst = kind == 0 ? q_out + ((int64_t)b * Hq + hh) * D
                        : k_cache + (((int64_t)b * Hkv + hh) * L + pos) * D;
 #pragma unroll
@@ -190,28 +211,86 @@ __global__ void __launch_bounds__(256) k_qk_norm_rope(const T *q, const T *k, co
 // processed in batches of 8 per warp with independent loads (the cache reads
 // are latency-bound at decode sizes), scores of all G heads live in shared
 // memory, softmax and the weighted sum of values run in fp32.
-template <typename T, int D, int G>
-__global__ void __launch_bounds__(D) k_attn_decode(const T *q, const T *k_cache, const T *v_cache,
+// ROPE: the CTA first does the q/k norm + rope + cache write of its own heads
+// (the G query heads, the kv head's new k and v row at `pos`), keeping the
+// rotated queries in shared memory; the cache row it writes is then read back
+// by the same CTA after a barrier.  A position outside the cache gives a zero
+// output and writes nothing.
+template <typename T> struct AttnRope {
+    const T *k, *v;                    // this step's k / v projections [B, Hkv, D]
+    const float *qw, *kw;              // per-head norm weights [D] (may be null)
+    const float *cosT, *sinT;          // [L, D]
+    float eps;
+};
+
+template <typename T, int D, int G, bool ROPE>
+__global__ void __launch_bounds__(D) k_attn_decode(const T *q, T *k_cache, T *v_cache,
                                                    const int64_t *pos_dev, int Hq, int Hkv, int64_t L,
-                                                   float scale, T *out) {
+                                                   float scale, T *out, const AttnRope<T> rp) {
     constexpr int NW = D / 32, E = D / 32, KB = 8;
     extern __shared__ float sc[];                 // scores [G][L]
     __shared__ float red[G][NW];
     __shared__ float stat[G][2];                  // max, sum
+    __shared__ float qs[ROPE ? G : 1][D];         // ROPE: the rotated queries
     pdl_launch_dependents();
     pdl_wait();
     const int bg = blockIdx.x;
     const int b = bg / Hkv, g = bg - b * Hkv;
-    const int64_t n = min(*pos_dev + 1, L);            // keys 0..pos (none if pos < 0)
+    const int64_t pos = *pos_dev;
+    int64_t n = min(pos + 1, L);                       // keys 0..pos (none if pos < 0)
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (ROPE) {
+        if (pos >= L) n = 0;
+        if (n > 0) {
+            // warp w takes heads w, w + NW, ... of the G query heads, k, v; all
+            // its loads (and the position's cos / sin) are issued first
+            constexpr int R = (G + 2 + NW - 1) / NW;
+            const T *kp = rp.k, *vp = rp.v;
+            const float *qw = rp.qw, *kw = rp.kw;
+            float xs[R][E], c[E], sn[E];
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int hh = warp + NW * r;
+                if (hh < G + 2) {
+                    const T *src = hh < G ? q + ((int64_t)b * Hq + g * G + hh) * D
+                                          : (hh == G ? kp : vp) + ((int64_t)b * Hkv + g) * D;
+#pragma unroll
+                    for (int e = 0; e < E; ++e) xs[r][e] = ld(src, lane * E + e);
+                }
+            }
+            rope_row<T, E>(rp.cosT + pos * D, rp.sinT + pos * D, lane, c, sn);
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int hh = warp + NW * r;
+                if (hh >= G + 2) break;
+                if (hh == G + 1) {
+                    T *dst = v_cache + (((int64_t)b * Hkv + g) * L + pos) * D;
+#pragma unroll
+                    for (int e = 0; e < E; ++e) dst[lane * E + e] = from_f32<T>(xs[r][e]);
+                    continue;
+                }
+                float o[E];
+                qk_head<T, E>(xs[r], rp.eps, hh < G ? qw : kw, c, sn, lane, o);
+                if (hh < G) {
+#pragma unroll
+                    for (int e = 0; e < E; ++e) qs[hh][lane * E + e] = o[e];
+                } else {
+                    T *dst = k_cache + (((int64_t)b * Hkv + g) * L + pos) * D;
+#pragma unroll
+                    for (int e = 0; e < E; ++e) dst[lane * E + e] = from_f32<T>(o[e]);
+                }
+            }
+        }
+        __syncthreads();                              // rotated queries and the new cache row
+    }
     float qv[G][E];
 #pragma unroll
     for (int h = 0; h < G; ++h) {
         const T *qr = q + ((int64_t)b * Hq + g * G + h) * D;
 #pragma unroll
-        for (int e = 0; e < E; ++e) qv[h][e] = ld(qr, lane * E + e);
+        for (int e = 0; e < E; ++e) qv[h][e] = ROPE ? qs[h][lane * E + e] : ld(qr, lane * E + e);
     }
-    const T *kb = k_cache + ((int64_t)b * Hkv + g) * L * D;
+    const T *kb = k_cache + ((int64_t)b * Hkv + g) * L * D;     // same pointer as the writes above
     const T *vb = v_cache + ((int64_t)b * Hkv + g) * L * D;
     float mx[G];
 #pragma unroll
@@ -378,29 +457,37 @@ extern "C" int cbq_qk_norm_rope(const void *q_dev, const void *k_dev, const void
     return CBQ_OK;
 }
 
-extern "C" int cbq_attn_decode(const void *q_dev, const void *k_cache_dev, const void *v_cache_dev, int dtype,
-                               int64_t B, int64_t Hq, int64_t Hkv, int64_t head_dim, int64_t cache_len,
-                               const int64_t *pos_dev, float scale, void *out_dev, void *stream) {
+namespace {
+
+template <bool ROPE>
+int launch_attn(const void *q_dev, void *k_cache_dev, void *v_cache_dev, int dtype, int64_t B, int64_t Hq,
+                int64_t Hkv, int64_t head_dim, int64_t cache_len, const int64_t *pos_dev, float scale,
+                void *out_dev, const void *k_dev, const void *v_dev, const float *qw, const float *kw,
+                const float *cos_dev, const float *sin_dev, float eps, void *stream) {
     if (B < 0 || Hq < 1 || Hkv < 1 || Hq % Hkv || cache_len < 1 || (dtype != CBQ_F32 && dtype != CBQ_BF16))
         return CBQ_ERR_ARG;
     if (head_dim != 64 && head_dim != 128 && head_dim != 256) return CBQ_ERR_UNSUPPORTED;
     const int64_t G = Hq / Hkv;
     if (G < 1 || G > 8) return CBQ_ERR_UNSUPPORTED;
     const size_t smem = (size_t)cache_len * 4 * (size_t)G;       // scores of the group's heads
-    if (smem > (size_t)cbq_host::max_smem_optin() - 4096) return CBQ_ERR_UNSUPPORTED;
+    if (smem > (size_t)cbq_host::max_smem_optin() - 4096 - (ROPE ? (size_t)G * head_dim * 4 : 0))
+        return CBQ_ERR_UNSUPPORTED;
     if (B == 0) return CBQ_OK;
     if (!q_dev || !k_cache_dev || !v_cache_dev || !pos_dev || !out_dev || B * Hkv > 0x7fffffff) return CBQ_ERR_ARG;
+    if (ROPE && (!k_dev || !v_dev || !cos_dev || !sin_dev)) return CBQ_ERR_ARG;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const dim3 grid((unsigned)(B * Hkv));
 #define CBQ_AT(T, D, GG)                                                                             \
     do {                                                                                             \
-        if (smem > 48 * 1024)                                                                        \
-            CBQ_CUDA_TRY(cudaFuncSetAttribute(k_attn_decode<T, D, GG>,                               \
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
-        CBQ_CUDA_TRY(cbq_host::launch_pdl(k_attn_decode<T, D, GG>, grid, dim3(D), smem, s,           \
-                                          static_cast<const T *>(q_dev), static_cast<const T *>(k_cache_dev), \
-                                          static_cast<const T *>(v_cache_dev), pos_dev, (int)Hq, (int)Hkv, \
-                                          cache_len, scale, static_cast<T *>(out_dev)));             \
+        auto kern = k_attn_decode<T, D, GG, ROPE>;                                                   \
+        if (smem > 32 * 1024)                                                                        \
+            CBQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
+        const AttnRope<T> rp{static_cast<const T *>(k_dev), static_cast<const T *>(v_dev), qw, kw,  \
+                             cos_dev, sin_dev, eps};                                                 \
+        CBQ_CUDA_TRY(cbq_host::launch_pdl(kern, grid, dim3(D), smem, s, static_cast<const T *>(q_dev), \
+                                          static_cast<T *>(k_cache_dev), static_cast<T *>(v_cache_dev), \
+                                          pos_dev, (int)Hq, (int)Hkv, cache_len, scale,              \
+                                          static_cast<T *>(out_dev), rp));                           \
     } while (0)
 #define CBQ_AT_G(T, D)                                                                               \
     do {                                                                                             \
@@ -427,4 +514,26 @@ extern "C" int cbq_attn_decode(const void *q_dev, const void *k_cache_dev, const
 #undef CBQ_AT
     CBQ_CUDA_TRY(cudaGetLastError());
     return CBQ_OK;
+}
+
+}  // namespace
+
+extern "C" int cbq_attn_decode(const void *q_dev, const void *k_cache_dev, const void *v_cache_dev, int dtype,
+                               int64_t B, int64_t Hq, int64_t Hkv, int64_t head_dim, int64_t cache_len,
+                               const int64_t *pos_dev, float scale, void *out_dev, void *stream) {
+    // the kernel only reads the cache in this form
+    return launch_attn<false>(q_dev, const_cast<void *>(k_cache_dev), const_cast<void *>(v_cache_dev), dtype, B,
+                              Hq, Hkv, head_dim, cache_len, pos_dev, scale, out_dev, nullptr, nullptr, nullptr,
+                              nullptr, nullptr, nullptr, 0.f, stream);
+}
+
+extern "C" int cbq_attn_decode_rope(const void *q_dev, const void *k_dev, const void *v_dev, int dtype, int64_t B,
+                                    int64_t Hq, int64_t Hkv, int64_t head_dim, float eps,
+                                    const float *q_weight_dev, const float *k_weight_dev, const float *cos_dev,
+                                    const float *sin_dev, const int64_t *pos_dev, void *k_cache_dev,
+                                    void *v_cache_dev, int64_t cache_len, float scale, void *out_dev,
+                                    void *stream) {
+    return launch_attn<true>(q_dev, k_cache_dev, v_cache_dev, dtype, B, Hq, Hkv, head_dim, cache_len, pos_dev,
+                             scale, out_dev, k_dev, v_dev, q_weight_dev, k_weight_dev, cos_dev, sin_dev, eps,
+                             stream);
 }

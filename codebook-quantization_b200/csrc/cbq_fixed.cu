@@ -332,11 +332,13 @@ extern "C" int cbq_linear_fixed_multi(const void *x_dev, int x_dtype, int64_t T,
                        static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int cbq_linear_fixed_peer(const void *x_dev, int x_dtype, int64_t T, int64_t ldx,
-                                     const uint8_t *packed_dev, int64_t packed_bytes, const float *codebook_dev,
-                                     int64_t C, int bits, int64_t M, int64_t K, const float *bias_dev, int world,
-                                     void *const *slot_dev, uint32_t *const *count_dev, int64_t ldo, int out_dtype,
-                                     void *stream) {
+namespace {
+
+// GemvArgs of the one-matrix peer-partial GEMV (cbq_linear_fixed_peer*).
+int peer_args(const void *x_dev, int x_dtype, int64_t T, int64_t ldx, const uint8_t *packed_dev,
+              int64_t packed_bytes, const float *codebook_dev, int64_t C, int bits, int64_t M, int64_t K,
+              const float *bias_dev, int world, void *const *slot_dev, uint32_t *const *count_dev, int64_t ldo,
+              int out_dtype, GemvArgs &a, GemvPlan &g) {
     if (world < 1 || world > kGvMaxPeers || !slot_dev || !count_dev) return CBQ_ERR_ARG;
     if (T < 1 || M < 1 || K < 1 || bits < 1 || bits > 16 || C < 1 || C > 65536 || ldo < M) return CBQ_ERR_ARG;
     if ((x_dtype != CBQ_F32 && x_dtype != CBQ_BF16) || (out_dtype != CBQ_F32 && out_dtype != CBQ_BF16))
@@ -348,9 +350,8 @@ extern "C" int cbq_linear_fixed_peer(const void *x_dev, int x_dtype, int64_t T, 
     const int xbytes = x_dtype == CBQ_BF16 ? 2 : 4;
     if ((reinterpret_cast<uintptr_t>(x_dev) & 15) || (ldx * xbytes) % 16 || (reinterpret_cast<uintptr_t>(packed_dev) & 15))
         return CBQ_ERR_UNSUPPORTED;
-    GemvPlan g;
     if (!plan_gemv(M, K, bits, C, T, g)) return CBQ_ERR_UNSUPPORTED;
-    GemvArgs a{};
+    a = GemvArgs{};
     a.x = x_dev; a.ldx = ldx; a.t0 = 0; a.ntok = (int)T; a.codebook = codebook_dev;
     a.C = (int)C; a.M = (int)M; a.K = (int)K; a.nseg = g.nseg; a.rows_per_cta = g.rows_per_cta;
     a.nmat = 1; a.epi = kEpiPeer;
@@ -362,6 +363,77 @@ extern "C" int cbq_linear_fixed_peer(const void *x_dev, int x_dtype, int64_t T, 
         a.peers.slot[p] = slot_dev[p];
         a.peers.count[p] = count_dev[p];
     }
+    return CBQ_OK;
+}
+
+}  // namespace
+
+extern "C" int cbq_linear_fixed_peer(const void *x_dev, int x_dtype, int64_t T, int64_t ldx,
+                                     const uint8_t *packed_dev, int64_t packed_bytes, const float *codebook_dev,
+                                     int64_t C, int bits, int64_t M, int64_t K, const float *bias_dev, int world,
+                                     void *const *slot_dev, uint32_t *const *count_dev, int64_t ldo, int out_dtype,
+                                     void *stream) {
+    GemvArgs a;
+    GemvPlan g;
+    const int rc = peer_args(x_dev, x_dtype, T, ldx, packed_dev, packed_bytes, codebook_dev, C, bits, M, K, bias_dev,
+                             world, slot_dev, count_dev, ldo, out_dtype, a, g);
+    if (rc != CBQ_OK) return rc;
+    return launch_gemv(bits, (int)T, g.nf, x_dtype == CBQ_BF16, a, g.smem, g.grid,
+                       static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int cbq_linear_fixed_peer_norm(const void *x_dev, int x_dtype, int64_t T, int64_t ldx,
+                                          const uint8_t *packed_dev, int64_t packed_bytes,
+                                          const float *codebook_dev, int64_t C, int bits, int64_t M, int64_t K,
+                                          const float *bias_dev, int world, void *const *slot_dev,
+                                          uint32_t *const *count_dev, int64_t ldo, int out_dtype,
+                                          const void *local_slots_dev, const uint32_t *local_counts_dev,
+                                          const uint32_t *epoch_dev, int64_t expect, void *resid_dev, int64_t ldr,
+                                          const float *norm_weight_dev, float eps, void *norm_out_dev, int64_t ldn,
+                                          uint32_t *arrive_dev, uint32_t *status_dev, void *stream) {
+    GemvArgs a;
+    GemvPlan g;
+    const int rc = peer_args(x_dev, x_dtype, T, ldx, packed_dev, packed_bytes, codebook_dev, C, bits, M, K, bias_dev,
+                             world, slot_dev, count_dev, ldo, out_dtype, a, g);
+    if (rc != CBQ_OK) return rc;
+    if (!local_slots_dev || !local_counts_dev || !epoch_dev || !resid_dev || !norm_out_dev || !arrive_dev ||
+        expect < 1 || expect > 0xffffffffll || ldr < M || ldn < M)
+        return CBQ_ERR_ARG;
+    a.status = status_dev;
+    a.norm = GemvNorm{arrive_dev, norm_weight_dev, eps, norm_out_dev, ldn, resid_dev, ldr, local_slots_dev,
+                      local_counts_dev, epoch_dev, (uint32_t)expect};
+    return launch_gemv(bits, (int)T, g.nf, x_dtype == CBQ_BF16, a, g.smem, g.grid,
+                       static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int cbq_linear_fixed_residual_norm(const void *x_dev, int x_dtype, int64_t T, int64_t ldx,
+                                              const uint8_t *packed_dev, int64_t packed_bytes,
+                                              const float *codebook_dev, int64_t C, int bits, int64_t M,
+                                              int64_t K, const float *bias_dev, void *resid_dev, int64_t ldr,
+                                              int out_dtype, const float *norm_weight_dev, float eps,
+                                              void *norm_out_dev, int64_t ldn, uint32_t *arrive_dev,
+                                              void *stream) {
+    if (T < 1 || M < 1 || K < 1 || bits < 1 || bits > 16 || C < 1 || C > 65536 || ldr < M || ldn < M)
+        return CBQ_ERR_ARG;
+    if ((x_dtype != CBQ_F32 && x_dtype != CBQ_BF16) || (out_dtype != CBQ_F32 && out_dtype != CBQ_BF16))
+        return CBQ_ERR_ARG;
+    if (!x_dev || !packed_dev || !codebook_dev || !resid_dev || !norm_out_dev || !arrive_dev || ldx < K)
+        return CBQ_ERR_ARG;
+    if (packed_bytes < cbq_fixed_stream_bytes(M, K, bits)) return CBQ_ERR_ARG;
+    const int xbytes = x_dtype == CBQ_BF16 ? 2 : 4;
+    if ((reinterpret_cast<uintptr_t>(x_dev) & 15) || (ldx * xbytes) % 16 || (reinterpret_cast<uintptr_t>(packed_dev) & 15))
+        return CBQ_ERR_UNSUPPORTED;
+    GemvPlan g;
+    if (!plan_gemv(M, K, bits, C, T, g)) return CBQ_ERR_UNSUPPORTED;
+    GemvArgs a{};
+    a.x = x_dev; a.ldx = ldx; a.t0 = 0; a.ntok = (int)T; a.codebook = codebook_dev;
+    a.C = (int)C; a.M = (int)M; a.K = (int)K; a.nseg = g.nseg; a.rows_per_cta = g.rows_per_cta;
+    a.nmat = 1; a.epi = kEpiResidual;
+    a.mat[0] = GemvMat{packed_dev, resid_dev, bias_dev, resid_dev, ldr, (int)M};
+    a.out_bf16 = out_dtype == CBQ_BF16;
+    a.H = g.H; a.NP = g.NP; a.m128 = 128u; a.m4 = 4u; a.status = nullptr;
+    a.norm = GemvNorm{arrive_dev, norm_weight_dev, eps, norm_out_dev, ldn, resid_dev, ldr, nullptr, nullptr,
+                      nullptr, 0u};
     return launch_gemv(bits, (int)T, g.nf, x_dtype == CBQ_BF16, a, g.smem, g.grid,
                        static_cast<cudaStream_t>(stream));
 }

@@ -85,6 +85,27 @@ struct GemvPeers {
     int world;
 };
 
+// Optional RMSNorm of the launch's updated rows (kEpiResidual with one
+// matrix, or kEpiPeer), done by the CTA that finishes last: every CTA fences
+// its stores and counts itself on `arrive`; the one that brings the count to
+// the number of CTAs normalizes the T rows of n = M values (for kEpiPeer after
+// waiting, bounded, for every rank's partial rows in this rank's slots and
+// adding them to the residual stream in rank order) and resets the count.
+// Values equal cbq_rmsnorm / cbq_rmsnorm_allreduce (same reduction order).
+struct GemvNorm {
+    uint32_t *arrive;          // null: no norm
+    const float *w;            // norm weight [M] (may be null)
+    float eps;
+    void *out;                 // [T, ldn] normalized rows, output dtype
+    int64_t ldn;
+    void *resid;               // the residual stream [T, ldr] (kEpiResidual: mat[0].out)
+    int64_t ldr;
+    const void *slots;         // kEpiPeer: this rank's slots, slot p row t at (p * T + t) * ldo
+    const uint32_t *counts;    // kEpiPeer: this rank's arrival counters [world]
+    const uint32_t *epoch;     // kEpiPeer: counters are complete at epoch * expect
+    uint32_t expect;
+};
+
 struct GemvArgs {
     const void *x;
     int64_t ldx;
@@ -103,7 +124,138 @@ struct GemvArgs {
     uint32_t m128, m4;   // 128 and 4
     uint32_t *status;
     GemvPeers peers;     // kEpiPeer only
+    GemvNorm norm;
 };
+
+// The norm of GemvNorm, run by the last CTA (all its threads).  red: 16
+// floats of free shared memory.
+__device__ __forceinline__ void gv_norm_last(const GemvArgs &a, float *red) {
+    const GemvNorm &nm = a.norm;
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const bool bf = a.out_bf16 != 0;
+    const bool peer = a.epi == kEpiPeer;
+    const int64_t n = a.M;
+    auto ldv = [&](const void *p, int64_t i) -> float {             // L2: written by other CTAs / ranks
+        return bf ? __bfloat162float(__ldcg(static_cast<const __nv_bfloat16 *>(p) + i))
+                  : __ldcg(static_cast<const float *>(p) + i);
+    };
+    auto stv = [&](void *p, int64_t i, float v) {
+        if (bf) static_cast<__nv_bfloat16 *>(p)[i] = __float2bfloat16_rn(v);
+        else static_cast<float *>(p)[i] = v;
+    };
+    auto rnd = [&](float v) { return bf ? __bfloat162float(__float2bfloat16_rn(v)) : v; };
+    __shared__ int late;
+    if (peer) {
+        // a wait that already gave up in this run: do not wait again
+        if (tid == 0)
+            late = (a.status && (*(volatile uint32_t *)(a.status + CBQ_STATUS_FLAGS) & CBQ_FLAG_TIMEOUT)) ? 1 : 0;
+        __syncthreads();
+        if (!late && tid < a.peers.world) {
+            const uint32_t want = *nm.epoch * nm.expect;
+            const uint64_t t0 = global_timer_ns();
+            while (true) {
+                uint32_t c;
+                asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(c) : "l"(nm.counts + tid) : "memory");
+                if ((int32_t)(c - want) >= 0) break;
+                if (global_timer_ns() - t0 > kWaitNs) {
+                    late = 1;
+                    break;
+                }
+                __nanosleep(64);
+            }
+        }
+        __syncthreads();
+        if (late) {
+            if (tid == 0) {
+                report(a.status, CBQ_FLAG_TIMEOUT, 0u);
+                *nm.arrive = 0u;
+            }
+            return;
+        }
+        __threadfence_system();
+    } else {
+        __threadfence();
+    }
+    const int64_t ldo = a.mat[0].ldo;
+    // Thread i < 256 takes elements i, i + 256, ... in that order (the order
+    // of cbq_rmsnorm's kernel, so the sums are the same), kNV of them per
+    // pass with every load issued before any is used; rows of up to
+    // 256 * kNV values stay in registers for the normalising pass.
+    constexpr int kNV = 16;
+    for (int t = 0; t < a.ntok; ++t) {
+        void *xr = static_cast<uint8_t *>(nm.resid) + (a.t0 + t) * nm.ldr * (bf ? 2 : 4);
+        float ss = 0.f;
+        float keep[kNV];
+        if (tid < 256) {
+            for (int64_t base = 0; base < n; base += 256 * kNV) {
+                float v[kNV];
+#pragma unroll
+                for (int j = 0; j < kNV; ++j) {
+                    const int64_t i = base + tid + 256 * j;
+                    v[j] = i < n ? ldv(xr, i) : 0.f;
+                }
+                if (peer) {
+                    float sum[kNV];
+#pragma unroll
+                    for (int j = 0; j < kNV; ++j) sum[j] = 0.f;
+                    for (int p = 0; p < a.peers.world; ++p) {
+                        const int64_t so = ((int64_t)p * a.ntok + t) * ldo;
+#pragma unroll
+                        for (int j = 0; j < kNV; ++j) {
+                            const int64_t i = base + tid + 256 * j;
+                            if (i < n) sum[j] += ldv(nm.slots, so + i);
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < kNV; ++j) {
+                        const int64_t i = base + tid + 256 * j;
+                        if (i < n) {
+                            v[j] = rnd(v[j] + rnd(sum[j]));
+                            stv(xr, i, v[j]);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < kNV; ++j) {
+                    if (base + tid + 256 * j < n) ss += v[j] * v[j];
+                    keep[j] = v[j];
+                }
+            }
+        }
+        ss = warp_sum(ss);
+        if (lane == 0 && w < 8) red[w] = ss;
+        __syncthreads();
+        if (w == 0) {
+            float t2 = lane < 8 ? red[lane] : 0.f;
+            t2 = warp_sum(t2);
+            if (lane == 0) red[8] = t2;
+        }
+        __syncthreads();
+        const float scale = rsqrtf(red[8] / (float)n + nm.eps);
+        void *orow = static_cast<uint8_t *>(nm.out) + (a.t0 + t) * nm.ldn * (bf ? 2 : 4);
+        if (n <= 256 * kNV) {
+            if (tid < 256) {
+#pragma unroll
+                for (int j = 0; j < kNV; ++j) {
+                    const int64_t i = tid + 256 * j;
+                    if (i < n) {
+                        float v = rnd(keep[j] * scale);
+                        if (nm.w) v = nm.w[i] * v;
+                        stv(orow, i, v);
+                    }
+                }
+            }
+        } else {
+            for (int64_t i = tid; i < n; i += blockDim.x) {
+                float v = rnd(ldv(xr, i) * scale);
+                if (nm.w) v = nm.w[i] * v;
+                stv(orow, i, v);
+            }
+        }
+        __syncthreads();                                   // red[] reuse
+    }
+    if (tid == 0) *nm.arrive = 0u;
+}
 
 // Row v of the launch's row space -> (matrix, row of that matrix).  Rows are
 // the matrices' rows one after another, or (kEpiSiluMul) interleaved so that
@@ -463,6 +615,17 @@ __global__ void __launch_bounds__(kGvWarps * 32, 1) k_gemv_fixed(const GemvArgs 
                 store(mt, o, v);
             }
         }
+    }
+    if (a.norm.arrive) {
+        __shared__ int last;
+        __threadfence();                                   // this CTA's rows, before its count
+        __syncthreads();
+        if (tid == 0) {
+            const uint32_t nct = (uint32_t)((a.M + a.rows_per_cta - 1) / a.rows_per_cta);
+            last = atomicAdd(a.norm.arrive, 1u) == nct - 1u;
+        }
+        __syncthreads();
+        if (last) gv_norm_last(a, part);                   // the segment sums are consumed
     }
 }
 

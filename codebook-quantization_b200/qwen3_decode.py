@@ -49,11 +49,12 @@ class _PeerAllReduce:
     down_proj of each layer) a slot per rank ([world][B][hidden] in the
     activation dtype) and an arrival counter per rank.  Rank s's GEMV writes
     its partial product into slot s of every rank and adds its rows to every
-    rank's counter s (``cbq_linear_fixed_peer``); each rank's
-    ``cbq_rmsnorm_allreduce`` waits for epoch * hidden rows from every rank,
-    adds the slots in rank order into the residual stream and normalises.
-    Counters only grow (``epoch`` counts the steps), so nothing is reset
-    between steps."""
+    rank's counter s; the last CTA of each rank's GEMV waits for epoch * hidden
+    rows from every rank, adds the slots in rank order into the residual
+    stream and normalises (``cbq_linear_fixed_peer_norm``, one launch; with
+    ``fuse_norm=False`` the split pair ``cbq_linear_fixed_peer`` +
+    ``cbq_rmsnorm_allreduce``).  Counters only grow (``epoch`` counts the
+    steps), so nothing is reset between steps."""
 
     def __init__(self, dec, sites: int):
         import ctypes as ct
@@ -88,6 +89,16 @@ class _PeerAllReduce:
         dec = self.dec
         W = self.W
         stream = device_stream(dec.dev)
+        if dec.fuse_norm:
+            rc = _lib.lib().cbq_linear_fixed_peer_norm(
+                x.data_ptr(), dec.code, dec.B, x.shape[1], lin.packed.data_ptr(), lin.nbytes,
+                lin.codebook.data_ptr(), lin.C, lin.bits, lin.M, lin.K, None, W, self.slots[site], self.counts[site],
+                lin.M, dec.code, self.local + site * W * self.slot_bytes, self.local + self.data + site * W * 4,
+                self.epoch.data_ptr(), lin.M, dec.x.data_ptr(), dec.cfg.hidden, None, float(dec.cfg.rms_eps),
+                dec.h.data_ptr(), dec.cfg.hidden, dec.arrive.data_ptr(), self.status.data_ptr(), stream)
+            if rc != _lib.CBQ_OK:
+                raise _lib.CbqError("cbq_linear_fixed_peer_norm", rc)
+            return
         rc = _lib.lib().cbq_linear_fixed_peer(
             x.data_ptr(), dec.code, dec.B, x.shape[1], lin.packed.data_ptr(), lin.nbytes, lin.codebook.data_ptr(),
             lin.C, lin.bits, lin.M, lin.K, None, W, self.slots[site], self.counts[site], lin.M, dec.code, stream)
@@ -123,7 +134,7 @@ def _rms(x, eps):
 class Qwen3Decoder:
     def __init__(self, weights: CompressedQwen3Weights, batch: int, max_len: int,
                  act_dtype=torch.bfloat16, group: Optional[dist.ProcessGroup] = None, fused: bool = True,
-                 allreduce: str = "peer"):
+                 allreduce: str = "peer", fuse_norm: bool = False, fuse_rope: bool = True):
         self.w, self.cfg = weights, weights.cfg
         cfg = self.cfg
         self.dev = weights.device
@@ -148,14 +159,21 @@ class Qwen3Decoder:
         self.vocab_local = cfg.vocab // self.world
         self.ar = torch.arange(max_len, device=self.dev)
         self.fused = fused
+        # fused step: q/k norm + rope done by the attention launch, and
+        # optionally the RMSNorm done by the last CTA of the row-parallel GEMV
+        # before it (measured slower on a B200 than its own one-CTA launch,
+        # which waits on the SM the GEMV grid leaves free; off by default)
+        self.fuse_norm, self.fuse_rope = fuse_norm, fuse_rope
         if fused:
             hq, hkv = self.hl * d, self.kvl * d
             z = lambda n: torch.zeros(batch, n, dtype=act_dtype, device=self.dev)
             self.x, self.h, self.y = z(cfg.hidden), z(cfg.hidden), z(cfg.hidden)
             self.q, self.k, self.v = z(hq), z(hkv), z(hkv)
-            self.qn, self.a = z(hq), z(hq)
+            self.a, self.qn = z(hq), (None if fuse_rope else z(hq))
             self.m = z(cfg.inter // self.world)
             self.code = _lib.CBQ_BF16 if act_dtype == torch.bfloat16 else _lib.CBQ_F32
+            # arrival count of the GEMVs whose last CTA normalises (0 between launches)
+            self.arrive = torch.zeros(1, dtype=torch.int32, device=self.dev)
         self.peer = None
         if fused and self.world > 1 and allreduce == "peer" and not weights.huffman and batch <= 2:
             self.peer = _PeerAllReduce(self, 2 * cfg.layers)
@@ -205,6 +223,23 @@ class Qwen3Decoder:
                   x.shape[0], x.shape[1], None, float(self.cfg.rms_eps), out.data_ptr(),
                   device_stream(self.dev))
 
+    def _residual_norm(self, lin, x):
+        """self.x += x @ W^T, then self.h = RMSNorm(self.x): one launch
+        (``cbq_linear_fixed_residual_norm``, whose last CTA normalises) when the
+        fused kernel takes the layer, else the GEMV and ``cbq_rmsnorm``."""
+        if self.fuse_norm and isinstance(lin, GPUAcceleratedLinear):
+            rc = _lib.lib().cbq_linear_fixed_residual_norm(
+                x.data_ptr(), self.code, self.B, x.shape[1], lin.packed.data_ptr(), lin.nbytes,
+                lin.codebook.data_ptr(), lin.C, lin.bits, lin.M, lin.K, None, self.x.data_ptr(), self.x.shape[1],
+                self.code, None, float(self.cfg.rms_eps), self.h.data_ptr(), self.h.shape[1],
+                self.arrive.data_ptr(), device_stream(self.dev))
+            if rc == _lib.CBQ_OK:
+                return
+            if rc != _lib.CBQ_ERR_UNSUPPORTED:
+                raise _lib.CbqError("cbq_linear_fixed_residual_norm", rc)
+        self._linear((lin,), (self.x,), _lib.CBQ_EPI_RESIDUAL, (self.x,), x=x)
+        self._rmsnorm(self.x, self.h)
+
     def _linear(self, mats, outs, epilogue=_lib.CBQ_EPI_STORE, resids=None, x=None):
         x = self.h if x is None else x
         fixed = all(isinstance(m, GPUAcceleratedLinear) for m in mats)
@@ -230,16 +265,21 @@ class Qwen3Decoder:
         self._rmsnorm(self.x, self.h)
         for li, (q_p, k_p, v_p, o_p, g_p, u_p, d_p) in enumerate(self.layer_mods):
             self._linear((q_p, k_p, v_p), (self.q, self.k, self.v))
-            _lib.call("cbq_qk_norm_rope", self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(), self.code,
-                      B, self.hl, self.kvl, d, float(cfg.rms_eps), None, None, self.cos.data_ptr(),
-                      self.sin.data_ptr(), self.pos.data_ptr(), self.qn.data_ptr(),
-                      self.k_cache[li].data_ptr(), self.v_cache[li].data_ptr(), self.max_len, stream)
-            _lib.call("cbq_attn_decode", self.qn.data_ptr(), self.k_cache[li].data_ptr(),
-                      self.v_cache[li].data_ptr(), self.code, B, self.hl, self.kvl, d, self.max_len,
-                      self.pos.data_ptr(), float(d ** -0.5), self.a.data_ptr(), stream)
+            if self.fuse_rope:
+                _lib.call("cbq_attn_decode_rope", self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(),
+                          self.code, B, self.hl, self.kvl, d, float(cfg.rms_eps), None, None, self.cos.data_ptr(),
+                          self.sin.data_ptr(), self.pos.data_ptr(), self.k_cache[li].data_ptr(),
+                          self.v_cache[li].data_ptr(), self.max_len, float(d ** -0.5), self.a.data_ptr(), stream)
+            else:
+                _lib.call("cbq_qk_norm_rope", self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(), self.code,
+                          B, self.hl, self.kvl, d, float(cfg.rms_eps), None, None, self.cos.data_ptr(),
+                          self.sin.data_ptr(), self.pos.data_ptr(), self.qn.data_ptr(),
+                          self.k_cache[li].data_ptr(), self.v_cache[li].data_ptr(), self.max_len, stream)
+                _lib.call("cbq_attn_decode", self.qn.data_ptr(), self.k_cache[li].data_ptr(),
+                          self.v_cache[li].data_ptr(), self.code, B, self.hl, self.kvl, d, self.max_len,
+                          self.pos.data_ptr(), float(d ** -0.5), self.a.data_ptr(), stream)
             if self.world == 1:
-                self._linear((o_p,), (self.x,), _lib.CBQ_EPI_RESIDUAL, (self.x,), x=self.a)
-                self._rmsnorm(self.x, self.h)
+                self._residual_norm(o_p, self.a)
             elif self.peer is not None:
                 self.peer.run(2 * li, o_p, self.a)
             else:
@@ -248,8 +288,7 @@ class Qwen3Decoder:
                 self._rmsnorm(self.x, self.h, add=self.y)
             self._linear((g_p, u_p), (self.m,), _lib.CBQ_EPI_SILU_MUL)
             if self.world == 1:
-                self._linear((d_p,), (self.x,), _lib.CBQ_EPI_RESIDUAL, (self.x,), x=self.m)
-                self._rmsnorm(self.x, self.h)
+                self._residual_norm(d_p, self.m)
             elif self.peer is not None:
                 self.peer.run(2 * li + 1, d_p, self.m)
             else:
@@ -274,9 +313,16 @@ class Qwen3Decoder:
     def launches_per_step(self) -> int:
         """libcbq kernel launches in one step (embedding, linears, fused block kernels)."""
         n = self.cfg.layers
-        if self.fused:
-            return 2 + 8 * n + 1          # embedding + first RMSNorm, 8 per layer, lm_head
-        return 1 + 7 * n + 1              # embedding, 7 linears per layer, lm_head
+        if not self.fused:
+            return 1 + 7 * n + 1          # embedding, 7 linears per layer, lm_head
+        attn = 1 if self.fuse_rope else 2
+        if self.w.huffman or self.B > 2:  # one launch per linear, separate RMSNorms
+            per = 3 + attn + 1 + 2 + 1 + 2
+        elif (self.world == 1 or self.peer is not None) and self.fuse_norm:
+            per = 3 + attn                # q/k/v, attention, o (+norm), gate/up, down (+norm)
+        else:
+            per = 5 + attn                # separate RMSNorm launches (after NCCL at TP > 1)
+        return 2 + per * n + 1            # embedding + first RMSNorm, the layers, lm_head
 
     def step(self, ids: torch.Tensor, pos: int) -> torch.Tensor:
         """Eager step (no graph): returns the greedy next ids [B]."""

@@ -146,6 +146,39 @@ int cbq_linear_fixed_peer(const void *x_dev, int x_dtype, int64_t T, int64_t ldx
                           void *const *slot_dev, uint32_t *const *count_dev, int64_t ldo, int out_dtype,
                           void *stream);
 
+/* cbq_linear_fixed_peer followed, in the same launch, by what
+ * cbq_rmsnorm_allreduce does: the CTA that finishes last (counted on
+ * arrive_dev, a uint32 that is 0 before the call and left 0) waits, bounded,
+ * until local_counts_dev[s] >= *epoch_dev * expect for every rank s, then
+ * resid[t] = round(resid[t] + round(sum_s slot_s[t])) in rank order (slot s
+ * row t at local_slots_dev + (s * T + t) * ldo elements) and norm_out[t] =
+ * RMSNorm(resid[t]) with norm_weight_dev (may be NULL) and eps.  A wait that
+ * gives up sets CBQ_FLAG_TIMEOUT in status_dev, after which later calls do
+ * not wait.  One launch replaces the two of the unfused pair. */
+int cbq_linear_fixed_peer_norm(const void *x_dev, int x_dtype, int64_t T, int64_t ldx,
+                               const uint8_t *packed_dev, int64_t packed_bytes, const float *codebook_dev,
+                               int64_t C, int bits, int64_t M, int64_t K, const float *bias_dev, int world,
+                               void *const *slot_dev, uint32_t *const *count_dev, int64_t ldo, int out_dtype,
+                               const void *local_slots_dev, const uint32_t *local_counts_dev,
+                               const uint32_t *epoch_dev, int64_t expect, void *resid_dev, int64_t ldr,
+                               const float *norm_weight_dev, float eps, void *norm_out_dev, int64_t ldn,
+                               uint32_t *arrive_dev, uint32_t *status_dev, void *stream);
+
+/* cbq_linear_fixed_multi with CBQ_EPI_RESIDUAL for one matrix followed, in
+ * the same launch, by cbq_rmsnorm of the updated rows: resid[t] +=
+ * round(x[t] @ W^T (+ bias)) (resid [T, ldr], in place), then norm_out[t]
+ * (stride ldn) = RMSNorm(resid[t]) with norm_weight_dev (may be NULL) and
+ * eps, the values cbq_rmsnorm gives.  The CTA that finishes last (counted on
+ * arrive_dev: 0 before the call, left 0) normalizes the rows.  T <= 2 and the
+ * alignment rules of cbq_linear_fixed_multi, else CBQ_ERR_UNSUPPORTED before
+ * launching. */
+int cbq_linear_fixed_residual_norm(const void *x_dev, int x_dtype, int64_t T, int64_t ldx,
+                                   const uint8_t *packed_dev, int64_t packed_bytes, const float *codebook_dev,
+                                   int64_t C, int bits, int64_t M, int64_t K, const float *bias_dev,
+                                   void *resid_dev, int64_t ldr, int out_dtype, const float *norm_weight_dev,
+                                   float eps, void *norm_out_dev, int64_t ldn, uint32_t *arrive_dev,
+                                   void *stream);
+
 /* Size of the device array built into the library that
  * cbq_linear_fixed_noalloc uses as its workspace (8 MiB on every GPU that
  * loads the library, until the process exits). */
@@ -334,6 +367,17 @@ int cbq_qk_norm_rope(const void *q_dev, const void *k_dev, const void *v_dev, in
 int cbq_attn_decode(const void *q_dev, const void *k_cache_dev, const void *v_cache_dev, int dtype,
                     int64_t B, int64_t Hq, int64_t Hkv, int64_t head_dim, int64_t cache_len,
                     const int64_t *pos_dev, float scale, void *out_dev, void *stream);
+
+/* cbq_qk_norm_rope followed by cbq_attn_decode in one launch: q_dev, k_dev,
+ * v_dev are this step's projections; each CTA normalizes and rotates its kv
+ * head's query heads (kept on chip) and new k row, writes the new k and v
+ * rows at *pos_dev into the caches, then attends over rows 0..*pos_dev.  A
+ * position outside [0, cache_len) gives a zero output and writes nothing. */
+int cbq_attn_decode_rope(const void *q_dev, const void *k_dev, const void *v_dev, int dtype, int64_t B,
+                         int64_t Hq, int64_t Hkv, int64_t head_dim, float eps, const float *q_weight_dev,
+                         const float *k_weight_dev, const float *cos_dev, const float *sin_dev,
+                         const int64_t *pos_dev, void *k_cache_dev, void *v_cache_dev, int64_t cache_len,
+                         float scale, void *out_dev, void *stream);
 
 #ifdef __cplusplus
 }

@@ -166,3 +166,79 @@ def test_attn_decode_matches_sdpa(dt, d, pos):
     ref = (att @ vr).reshape(B, Hq * d)
     tol = 1e-5 if dt == torch.float32 else 8e-3
     assert rel_l2(out.float().cpu().numpy(), ref.cpu().numpy()) < tol
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+@pytest.mark.parametrize("d,G,pos", [(128, 4, 0), (128, 4, 57), (64, 3, 140), (128, 8, 9)])
+def test_attn_decode_rope_equals_the_two_launches(dt, d, G, pos):
+    """The fused launch (q/k norm + rope + cache write + attention) gives the
+    same output and cache rows, bit for bit, as cbq_qk_norm_rope followed by
+    cbq_attn_decode; a position outside the cache writes nothing and gives 0."""
+    dev = need_cuda()
+    qd = importlib.import_module("codebook-quantization_b200.qwen3_decode")
+    B, Hkv, Lc = 2, 2, 160
+    Hq = G * Hkv
+    cos, sin = qd.rope_tables(d, Lc, 1e6, dev)
+    q = torch.randn(B, Hq * d, device=dev).to(dt)
+    k = torch.randn(B, Hkv * d, device=dev).to(dt)
+    v = torch.randn(B, Hkv * d, device=dev).to(dt)
+    qw = torch.rand(d, device=dev) + 0.5
+    kw = torch.rand(d, device=dev) + 0.5
+    kc0 = torch.randn(B, Hkv, Lc, d, device=dev).to(dt)
+    vc0 = torch.randn(B, Hkv, Lc, d, device=dev).to(dt)
+    p = torch.tensor([pos], device=dev)
+    code = L.CBQ_BF16 if dt == torch.bfloat16 else L.CBQ_F32
+    st = torch.cuda.current_stream(dev).cuda_stream
+    kc1, vc1 = kc0.clone(), vc0.clone()
+    qn = torch.empty(B, Hq, d, device=dev, dtype=dt)
+    ref = torch.empty(B, Hq * d, device=dev, dtype=dt)
+    L.call("cbq_qk_norm_rope", q.data_ptr(), k.data_ptr(), v.data_ptr(), code, B, Hq, Hkv, d, 1e-6, qw.data_ptr(),
+           kw.data_ptr(), cos.data_ptr(), sin.data_ptr(), p.data_ptr(), qn.data_ptr(), kc1.data_ptr(),
+           vc1.data_ptr(), Lc, st)
+    L.call("cbq_attn_decode", qn.data_ptr(), kc1.data_ptr(), vc1.data_ptr(), code, B, Hq, Hkv, d, Lc, p.data_ptr(),
+           d ** -0.5, ref.data_ptr(), st)
+    kc2, vc2 = kc0.clone(), vc0.clone()
+    out = torch.empty_like(ref)
+    L.call("cbq_attn_decode_rope", q.data_ptr(), k.data_ptr(), v.data_ptr(), code, B, Hq, Hkv, d, 1e-6,
+           qw.data_ptr(), kw.data_ptr(), cos.data_ptr(), sin.data_ptr(), p.data_ptr(), kc2.data_ptr(),
+           vc2.data_ptr(), Lc, d ** -0.5, out.data_ptr(), st)
+    assert torch.equal(kc2, kc1) and torch.equal(vc2, vc1)
+    assert torch.equal(out, ref)
+    p.fill_(Lc)
+    kc3, vc3 = kc0.clone(), vc0.clone()
+    L.call("cbq_attn_decode_rope", q.data_ptr(), k.data_ptr(), v.data_ptr(), code, B, Hq, Hkv, d, 1e-6,
+           qw.data_ptr(), kw.data_ptr(), cos.data_ptr(), sin.data_ptr(), p.data_ptr(), kc3.data_ptr(),
+           vc3.data_ptr(), Lc, d ** -0.5, out.data_ptr(), st)
+    torch.cuda.synchronize()
+    assert torch.equal(kc3, kc0) and torch.equal(vc3, vc0)
+    assert not bool(out.any())
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+@pytest.mark.parametrize("T,M,K", [(1, 4096, 4096), (2, 2048, 6144), (1, 1024, 512), (1, 6144, 1024)])
+def test_residual_norm_launch_equals_gemv_then_rmsnorm(dt, T, M, K):
+    """cbq_linear_fixed_residual_norm (the GEMV whose last CTA normalises)
+    gives the residual stream and normalised rows of the residual GEMV
+    followed by cbq_rmsnorm, bit for bit, and leaves its arrival count 0."""
+    dev = need_cuda()
+    (m,) = _mats(dev, [M], K, seed=3)
+    xin = torch.randn(T, K, device=dev).to(dt)
+    resid0 = torch.randn(T, M, device=dev).to(dt)
+    w = torch.rand(M, device=dev) + 0.5
+    code = L.CBQ_BF16 if dt == torch.bfloat16 else L.CBQ_F32
+    st = torch.cuda.current_stream(dev).cuda_stream
+    r1 = resid0.clone()
+    h1 = torch.empty(T, M, device=dev, dtype=dt)
+    assert G.linear_fixed_multi([m], xin, [r1], L.CBQ_EPI_RESIDUAL, [r1])
+    L.call("cbq_rmsnorm", r1.data_ptr(), None, code, T, M, w.data_ptr(), 1e-6, h1.data_ptr(), st)
+    arrive = torch.zeros(1, dtype=torch.int32, device=dev)
+    for _ in range(3):                                   # the count is reusable
+        r2 = resid0.clone()
+        h2 = torch.empty_like(h1)
+        L.call("cbq_linear_fixed_residual_norm", xin.data_ptr(), code, T, K, m.packed.data_ptr(), m.nbytes,
+               m.codebook.data_ptr(), m.C, m.bits, M, K, None, r2.data_ptr(), M, code, w.data_ptr(), 1e-6,
+               h2.data_ptr(), M, arrive.data_ptr(), st)
+        torch.cuda.synchronize()
+        assert torch.equal(r2, r1)
+        assert torch.equal(h2, h1)
+        assert int(arrive.item()) == 0

@@ -2,7 +2,7 @@
 those of the same model on one GPU (fp32 activations; only the summation order
 of the all-reduced partial products differs), with the row-parallel layers'
 all-reduce done by the fused peer-memory path (GEMV epilogue writes into every
-rank's slot, the RMSNorm kernel sums) or by NCCL.  Skipped on machines with
+rank's slot; the RMSNorm kernel, or the GEMV's last CTA, sums) or by NCCL.  Skipped on machines with
 fewer than two GPUs."""
 import os
 import socket
@@ -30,7 +30,7 @@ def _prompt():
     return torch.randint(0, CFG.vocab, (2, 12), generator=torch.Generator().manual_seed(8))
 
 
-def _rank_main(rank, world, port, fused, huffman, q, allreduce="peer"):
+def _rank_main(rank, world, port, fused, huffman, q, allreduce="peer", fuse_norm=False):
     try:
         sys.path[:0] = [str(REPO), str(REPO / "tests")]
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -45,7 +45,7 @@ def _rank_main(rank, world, port, fused, huffman, q, allreduce="peer"):
                                 timeout=timedelta(seconds=60))
         W = pkg.qwen3.CompressedQwen3Weights(CFG, dev, huffman=huffman, rank=rank, world=world, seed=3)
         dec = qd.Qwen3Decoder(W, batch=2, max_len=40, act_dtype=torch.float32, group=dist.group.WORLD,
-                              fused=fused, allreduce=allreduce)
+                              fused=fused, allreduce=allreduce, fuse_norm=fuse_norm)
         peer = dec.peer is not None
         eager = dec.generate(_prompt(), 12).cpu()
         dec.reset()
@@ -64,10 +64,11 @@ def _rank_main(rank, world, port, fused, huffman, q, allreduce="peer"):
         q.put((rank, f"{type(e).__name__}: {e}", None, None))
 
 
-@pytest.mark.parametrize("fused,allreduce", [(True, "peer"), (True, "nccl"), (False, "nccl")],
-                         ids=["fused-peer", "fused-nccl", "torch-ops"])
+@pytest.mark.parametrize("fused,allreduce,fuse_norm", [(True, "peer", False), (True, "peer", True),
+                                                      (True, "nccl", False), (False, "nccl", False)],
+                         ids=["fused-peer", "fused-peer-norm", "fused-nccl", "torch-ops"])
 @pytest.mark.parametrize("huffman", [False, True], ids=["fixed", "huffman"])
-def test_tp2_decode_matches_one_gpu(fused, allreduce, huffman):
+def test_tp2_decode_matches_one_gpu(fused, allreduce, fuse_norm, huffman):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import importlib
@@ -79,7 +80,8 @@ def test_tp2_decode_matches_one_gpu(fused, allreduce, huffman):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, fused, huffman, q, allreduce)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, fused, huffman, q, allreduce, fuse_norm))
+             for r in range(2)]
     for p in procs:
         p.start()
     res = {}
