@@ -319,9 +319,9 @@ class Qwen3Decoder:
         if self.w.huffman or self.B > 2:  # one launch per linear, separate RMSNorms
             per = 3 + attn + 1 + 2 + 1 + 2
         elif (self.world == 1 or self.peer is not None) and self.fuse_norm:
-            per = 3 + attn                # q/k/v, attention, o (+norm), gate/up, down (+norm)
+            per = 4 + attn                # q/k/v, attention, o (+norm), gate/up, down (+norm)
         else:
-            per = 5 + attn                # separate RMSNorm launches (after NCCL at TP > 1)
+            per = 6 + attn                # the same with two RMSNorm launches (after NCCL at TP > 1)
         return 2 + per * n + 1            # embedding + first RMSNorm, the layers, lm_head
 
     def step(self, ids: torch.Tensor, pos: int) -> torch.Tensor:
