@@ -17,15 +17,16 @@
 //   * the decode tables and the first units are loaded before the
 //     programmatic-dependent-launch wait, i.e. while the previous kernel on
 //     the stream finishes.
-// With a value-mode table whose two levels resolve every prefix (lossless
-// codebooks), a lane runs four branch-free decoders over its chunk, from its
-// codes 0, 16, 32 and 48 (the load-time quarter lengths): a
-// symbol costs one shared load from the 14-bit first level and a predicated
-// one from the second level.  Bit patterns that match no code decode through
-// guard entries as the reference does (symbol 0, one bit).  Other tables
-// (symbol payloads, prefixes left to the canonical search) take a
-// one-decoder loop whose second-level load is voted per symbol; a partial
-// last chunk of a row (K % 64 != 0) is decoded symbol by symbol.
+// With a value-mode table (lossless codebooks), a lane runs four branch-free
+// decoders over its chunk, from its codes 0, 16, 32 and 48 (the load-time
+// quarter lengths): a symbol costs one shared load from the 14-bit first level
+// and a predicated one from the second level; where some prefixes' second
+// level did not fit (very deep codes, e.g. a 151936-row lm_head), the lanes
+// that meet one take the canonical search under a per-step vote.  Bit
+// patterns that match no code decode through guard entries as the reference
+// does (symbol 0, one bit).  Symbol-payload tables take a one-decoder loop
+// whose second-level load is voted per symbol; a partial last chunk of a row
+// (K % 64 != 0) is decoded symbol by symbol.
 #pragma once
 #include "cbq_huff_kernel.cuh"
 
@@ -250,6 +251,20 @@ struct HgDec {
             "and.b32 t, %0, 128;\n\tsetp.ne.u32 q, t, 0;\n\t"
             "@q ld.shared.u32 %0, [%1];\n\t}" : "+r"(e) : "r"(a2));
     }
+    // A prefix whose second level did not fit in shared memory has entry 0:
+    // those lanes (rare: the longest codes of tables with very deep ones)
+    // take the canonical search, the others skip it together.
+    __device__ __forceinline__ void canon(uint32_t mask, const HuffSlow *hs, const uint16_t *gsyms,
+                                          const float *gcb, uint32_t cmax) {
+        if (__any_sync(mask, e == 0u)) {
+            if (e == 0u) {
+                int L;
+                uint32_t sym = huff_canonical(win, hs, gsyms, kHfLutBits + 1, L);
+                if (L == 0) { L = 1; sym = 0; }                  // the reference's guard
+                e = (__float_as_uint(__ldg(gcb + min(sym, cmax))) & 0xffff0000u) | (uint32_t)L;
+            }
+        }
+    }
     __device__ __forceinline__ float consume(float x, float acc) {
         const uint32_t wt = e & 0xffff0000u;
         const uint32_t len = e - wt;
@@ -266,16 +281,19 @@ struct HgDec {
     }
 };
 
-// The common case: a value-mode table with every prefix resolved by its two
-// levels, and the chunk in the ring.  Four independent decoders per lane,
+// The common case: a value-mode table and the chunk in the ring (CANON: some
+// prefixes were left to the canonical search, see HgDec::canon).  Four
+// independent decoders per lane,
 // from the chunk's codes 0, 16, 32 and 48 (the packed quarter lengths of the
 // load-time table), interleaved phase by phase against the same registers of
 // x: straight-line code whose four dependency chains (window, first- and
 // second-level loads) overlap.  The ring slot holds the unit plus 32 bytes,
 // so every word a decoder reads is inside the slot.
-template <typename XV>
+template <bool CANON, typename XV>
 __device__ __forceinline__ float hg_chunk_v2(uint32_t ws, uint32_t bit0, uint32_t quarters, const XV &xr,
-                                             uint32_t lut_s, uint32_t sub_s, uint32_t m4, uint32_t m16) {
+                                             uint32_t lut_s, uint32_t sub_s, uint32_t m4, uint32_t m16,
+                                             uint32_t mask, const HuffSlow *hs, const uint16_t *gsyms,
+                                             const float *gcb, uint32_t cmax) {
     constexpr int kQ = kHgNF / 4;
     HgDec d[4];
     uint32_t b = bit0;
@@ -291,6 +309,10 @@ __device__ __forceinline__ float hg_chunk_v2(uint32_t ws, uint32_t bit0, uint32_
         for (int j = 0; j < 4; ++j) d[j].look(lut_s, m4);
 #pragma unroll
         for (int j = 0; j < 4; ++j) d[j].resolve(sub_s, m4, m16);
+        if (CANON) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) d[j].canon(mask, hs, gsyms, gcb, cmax);
+        }
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[j] = d[j].consume(xr[j * kQ + q], acc[j]);
     }
@@ -345,7 +367,7 @@ __device__ __forceinline__ void hg_loop(const HgArgs &a, const uint32_t *lut, co
     const uint32_t *quarter = a.chunk + (int64_t)a.M * nch;
     auto lane_quarters = [&](int64_t r, int s) -> uint32_t {
         const int q = 32 * s + lane;
-        return (VALUE && !CANON && q < nch) ? quarter[r * nch + q] : 0u;
+        return (VALUE && q < nch) ? quarter[r * nch + q] : 0u;
     };
     auto unit_end = [&](int64_t r, int s) -> int64_t {
         if (32 * s + 32 < nch) return a.rbs[r] + (int64_t)a.chunk[r * nch + 32 * s + 32];
@@ -423,9 +445,9 @@ __device__ __forceinline__ void hg_loop(const HgArgs &a, const uint32_t *lut, co
                                             : reinterpret_cast<const uint32_t *>(a.stream);
             const uint32_t nw = b0 >= 0 ? a.cap / 4 : (uint32_t)min((int64_t)0xffffffff, a.stream_bytes / 4);
             const uint64_t pos = b0 >= 0 ? (uint64_t)(my_bit - 8 * b0) : (uint64_t)my_bit;
-            if (VALUE && !CANON && nsym == kHgNF && b0 >= 0) {
-                acc = hg_chunk_v2(smem_u32(wbase), (uint32_t)pos, my_quarters, xr, smem_u32(lut), smem_u32(sub),
-                                  a.m4, a.m16);
+            if (VALUE && nsym == kHgNF && b0 >= 0) {
+                acc = hg_chunk_v2<CANON>(smem_u32(wbase), (uint32_t)pos, my_quarters, xr, smem_u32(lut),
+                                         smem_u32(sub), a.m4, a.m16, fast_ring, hs, gsyms, a.codebook, cmax);
             } else if (nsym == kHgNF && b0 >= 0) {
                 HgBits<true> bb;
                 bb.init(wbase, nw, pos);
