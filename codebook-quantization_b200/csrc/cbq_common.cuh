@@ -132,6 +132,18 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 
 }  // namespace cbq
 
+namespace cbq {
+// How linear_fixed_impl (cbq_fixed.cu) treats the workspace it is given.
+enum WsMode : int {
+    kWsCallerZeroed = 0,   // kept zeroed by the kernels between calls (cbq_linear_fixed)
+    kWsClearFirst = 1,     // shared scratch: cleared before use, too small -> CBQ_ERR_ARG
+};
+int linear_fixed_impl(const void *x, int x_dtype, int64_t T, int64_t ldx, const uint8_t *packed,
+                      const float *cb, int64_t C, int bits, int64_t M, int64_t K, const float *bias,
+                      void *out, int out_dtype, int64_t ldo, void *ws, int64_t ws_bytes,
+                      cudaStream_t s, int ws_mode);
+}  // namespace cbq
+
 // Host-side helpers shared by the .cu files.
 namespace cbq_host {
 int sm_count();           // SMs of the current device (cached per device)

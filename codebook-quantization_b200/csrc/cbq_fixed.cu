@@ -199,10 +199,21 @@ int launch_bits(int bits, int TB, bool xbf16, const FixedArgs &a, size_t smem, i
     return CBQ_ERR_ARG;
 }
 
+}  // namespace
+
+namespace cbq {
+
+// The fixed-width dispatch behind cbq_linear_fixed and
+// cbq_linear_fixed_noalloc.  Only k_linear_fixed (3..63 tokens, or fp32
+// activations) uses the workspace.  ws_mode kWsCallerZeroed: `ws` (may be
+// null) is kept zeroed by the kernels, as cbq_linear_fixed promises its
+// caller; kWsClearFirst: `ws` is a shared array holding an earlier call's
+// bytes -- a call that needs more than ws_bytes returns CBQ_ERR_ARG before
+// launching, and the bytes it uses are cleared on `s` first.
 int linear_fixed_impl(const void *x, int x_dtype, int64_t T, int64_t ldx, const uint8_t *packed,
                       const float *cb, int64_t C, int bits, int64_t M, int64_t K, const float *bias,
                       void *out, int out_dtype, int64_t ldo, void *ws, int64_t ws_bytes,
-                      cudaStream_t s) {
+                      cudaStream_t s, int ws_mode) {
     FixedPlan p;
     const bool aligned = (reinterpret_cast<uintptr_t>(packed) & 15) == 0;
     const int xbytes = x_dtype == CBQ_BF16 ? 2 : 4;
@@ -228,7 +239,12 @@ int linear_fixed_impl(const void *x, int x_dtype, int64_t T, int64_t ldx, const 
         a.x = x; a.ldx = ldx; a.packed = packed; a.codebook = cb; a.C = (int)C;
         a.M = (int)M; a.K = (int)K; a.nseg = p.nseg; a.bias = bias; a.out = out; a.ldo = ldo;
         a.out_bf16 = out_dtype == CBQ_BF16; a.cb_bytes = p.cb_bytes; a.status = nullptr;
-        if (ws && ws_bytes >= workspace_bytes_for(M, K, T)) {
+        const int64_t need = workspace_bytes_for(M, K, T);
+        if (ws_mode == kWsClearFirst) {
+            if (!ws || ws_bytes < need) return CBQ_ERR_ARG;
+            CBQ_CUDA_TRY(cudaMemsetAsync(ws, 0, (size_t)need, s));
+        }
+        if (ws && ws_bytes >= need) {
             const int64_t pb = cbq_host::align_up(M * p.nseg * p.TB * 4, 256);
             a.part = static_cast<float *>(ws);
             a.cnt = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(ws) + pb);
@@ -256,7 +272,7 @@ int linear_fixed_impl(const void *x, int x_dtype, int64_t T, int64_t ldx, const 
     return CBQ_OK;
 }
 
-}  // namespace
+}  // namespace cbq
 
 // ------------------------------------------------------------------- C ABI
 
@@ -285,9 +301,9 @@ extern "C" int cbq_linear_fixed(const void *x_dev, int x_dtype, int64_t T, int64
     if (ldx < K || ldo < M) return CBQ_ERR_ARG;
     if (packed_bytes < cbq_fixed_stream_bytes(M, K, bits)) return CBQ_ERR_ARG;
     if (workspace_dev && workspace_bytes < workspace_bytes_for(M, K, T)) return CBQ_ERR_ARG;
-    return linear_fixed_impl(x_dev, x_dtype, T, ldx, packed_dev, codebook_dev, C, bits, M, K,
-                             bias_dev, out_dev, out_dtype, ldo, workspace_dev, workspace_bytes,
-                             static_cast<cudaStream_t>(stream));
+    return cbq::linear_fixed_impl(x_dev, x_dtype, T, ldx, packed_dev, codebook_dev, C, bits, M, K,
+                                  bias_dev, out_dev, out_dtype, ldo, workspace_dev, workspace_bytes,
+                                  static_cast<cudaStream_t>(stream), cbq::kWsCallerZeroed);
 }
 
 extern "C" int cbq_linear_fixed_multi(const void *x_dev, int x_dtype, int64_t T, int64_t ldx, int nmat,

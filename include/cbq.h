@@ -189,13 +189,17 @@ int cbq_linear_fixed_residual_norm(const void *x_dev, int x_dtype, int64_t T, in
  * hands it only inputs and outputs).  No counterpart in the reference.
  * Same arguments and result as cbq_linear_fixed, but the workspace comes from
  * the built-in array above; no cudaMalloc/cudaFree is ever called.
- *   - Returns CBQ_ERR_ARG when the matrix needs more workspace than
- *     CBQ_NOALLOC_SCRATCH_BYTES (cbq_linear_fixed_workspace_bytes(M, K, T)).
- *   - The first call on a device looks the array's device address up; make
- *     that first call before any stream capture on that device.
+ *   - Only the 3..63-token kernel (and fp32 activations at 64 tokens or
+ *     more) uses the array.  On that path a matrix that needs more than
+ *     CBQ_NOALLOC_SCRATCH_BYTES (cbq_linear_fixed_workspace_bytes(M, K, T))
+ *     returns CBQ_ERR_ARG before anything is launched, and the bytes it uses
+ *     are cleared on `stream` before the launch.  One or two tokens, and 64
+ *     or more bf16 tokens, run without it (no size limit, no clearing).
+ *   - The first call in a CUDA context looks the array's device address up
+ *     (the address is cached per context); make that first call before any
+ *     stream capture in that context.
  *   - All calls share the one array: calls that overlap on the GPU (different
- *     streams, or several host threads) race and give wrong results.  Each
- *     call clears the part it uses on its stream before launching. */
+ *     streams, or several host threads) race and give wrong results. */
 int cbq_linear_fixed_noalloc(const void *x_dev, int x_dtype, int64_t T, int64_t ldx,
                              const uint8_t *packed_dev, int64_t packed_bytes,
                              const float *codebook_dev, int64_t C, int bits,

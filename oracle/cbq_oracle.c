@@ -246,6 +246,19 @@ void orc_huff_embedding_f32(const int64_t *ids, int64_t T, const uint8_t *stream
     }
 }
 
+/* Threads for the next parallel regions started by the calling thread (the
+ * OpenMP runtime is shared with the reference's own object in the process, so
+ * this also sets the threads of its kernels).  Overrides OMP_NUM_THREADS,
+ * which launchers such as torchrun set to 1. */
+void orc_set_threads(int n)
+{
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
 /* Threads OpenMP will use (for reporting the CPU baseline's core count). */
 int orc_max_threads(void)
 {

@@ -64,6 +64,7 @@ def lib() -> ct.CDLL:
         L.orc_huff_linear_f32.argtypes = [_P] + huff + [_P, _P, _I64, _I64, _I64, _I64, _P, _I64, _I64]
         L.orc_huff_embedding_f32.argtypes = [_P, _I64] + huff + [_P, _P, _I64, _I64, _P]
         L.orc_max_threads.restype = _INT
+        L.orc_set_threads.argtypes = [_INT]
         _lib = L
     return _lib
 
@@ -229,5 +230,17 @@ def ref_huff_decode_weights(d, codebook, M, K):
     return out
 
 
-def set_threads(n: int) -> None:
+def host_cores() -> int:
+    """Cores this process may run on."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def set_threads(n: int) -> int:
+    """Use ``n`` OpenMP threads in the oracle and the reference object from
+    now on (whatever OMP_NUM_THREADS says); returns the count now in effect."""
     os.environ["OMP_NUM_THREADS"] = str(int(n))
+    lib().orc_set_threads(int(n))
+    return threads()

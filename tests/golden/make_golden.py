@@ -1,9 +1,9 @@
 """Generate the golden fixtures in this directory from the reference itself.
 
-Run in a container that has the reference tree (default ``/root/reference``,
-or ``$CBQ_REFERENCE``) after ``make -C oracle``::
+Run where the reference tree is present, with ``$CBQ_REFERENCE`` naming its
+root, after ``make -C oracle REF=$CBQ_REFERENCE``::
 
-    python tests/golden/make_golden.py
+    CBQ_REFERENCE=<reference root> python tests/golden/make_golden.py
 
 It imports the reference's own ``src/bitpack.py`` and
 ``src/huffman_codebook.py`` (read-only; no byte-code is written) and calls the
@@ -33,7 +33,9 @@ import numpy as np
 sys.dont_write_bytecode = True
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
-REF = Path(os.environ.get("CBQ_REFERENCE", "/root/reference"))
+if not os.environ.get("CBQ_REFERENCE"):
+    sys.exit("set CBQ_REFERENCE to the reference project's root directory")
+REF = Path(os.environ["CBQ_REFERENCE"])
 sys.path.insert(0, str(REF / "src"))
 sys.path.insert(0, str(REPO / "oracle"))
 
