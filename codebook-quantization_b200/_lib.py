@@ -34,6 +34,8 @@ SIGNATURES = {
                                 _INT, _I64, _P, _I64, _P]),
     "cbq_linear_fixed_multi": (_INT, [_P, _INT, _I64, _I64, _INT, _P, _P, _P, _P, _I64, _INT, _I64, _P,
                                       _P, _P, _P, _INT, _INT, _P]),
+    "cbq_linear_fixed_multi_norm": (_INT, [_P, _INT, _I64, _I64, _INT, _P, _P, _P, _P, _I64, _INT, _I64, _P,
+                                           _P, _P, _P, _INT, _INT, _P, ct.c_float, _P]),
     "cbq_linear_fixed_peer": (_INT, [_P, _INT, _I64, _I64, _P, _I64, _P, _I64, _INT, _I64, _I64, _P, _INT,
                                      _P, _P, _I64, _INT, _P]),
     "cbq_linear_fixed_peer_norm": (_INT, [_P, _INT, _I64, _I64, _P, _I64, _P, _I64, _INT, _I64, _I64, _P, _INT,
@@ -69,6 +71,11 @@ SIGNATURES = {
     "cbq_attn_decode": (_INT, [_P, _P, _P, _INT, _I64, _I64, _I64, _I64, _I64, _P, ct.c_float, _P, _P]),
     "cbq_attn_decode_rope": (_INT, [_P, _P, _P, _INT, _I64, _I64, _I64, _I64, ct.c_float, _P, _P, _P, _P, _P,
                                     _P, _P, _I64, ct.c_float, _P, _P]),
+    "cbq_attn_workspace_bytes": (_I64, [_I64, _I64, _I64, _I64, _I64]),
+    "cbq_attn_decode_rope_split": (_INT, [_P, _P, _P, _INT, _I64, _I64, _I64, _I64, ct.c_float, _P, _P, _P, _P,
+                                          _P, _P, _P, _I64, ct.c_float, _P, _P, _I64, _P]),
+    "cbq_attn_decode_split": (_INT, [_P, _P, _P, _INT, _I64, _I64, _I64, _I64, _I64, _P, ct.c_float, _P, _P,
+                                     _I64, _P]),
 }
 CBQ_EPI_STORE, CBQ_EPI_RESIDUAL, CBQ_EPI_SILU_MUL = 0, 1, 2
 

@@ -8,6 +8,8 @@
 // softmax scale d^-1/2).  Element-wise steps round to the activation dtype at
 // the same points as the unfused torch sequence; reductions (sum of squares,
 // softmax, the attention-weighted sum) accumulate in fp32.
+#include <algorithm>
+
 #include "cbq_common.cuh"
 
 namespace {
@@ -206,16 +208,22 @@ __global__ void __launch_bounds__(256) k_qk_norm_rope(const T *q, const T *k, co
 }
 
 // -------------------------------------------------------- decode attention
-// One CTA per (row b, kv head g) computes the G = Hq/Hkv query heads that
-// share the kv head, so every K and V row is read once.  D threads; keys are
-// processed in batches of 8 per warp with independent loads (the cache reads
-// are latency-bound at decode sizes), scores of all G heads live in shared
-// memory, softmax and the weighted sum of values run in fp32.
-// ROPE: the CTA first does the q/k norm + rope + cache write of its own heads
-// (the G query heads, the kv head's new k and v row at `pos`), keeping the
-// rotated queries in shared memory; the cache row it writes is then read back
-// by the same CTA after a barrier.  A position outside the cache gives a zero
-// output and writes nothing.
+// The keys 0..pos of one (row b, kv head g) are split over S CTAs
+// (flash-decoding): CTA (b, g, s) takes keys [s*c, min((s+1)*c, n)),
+// c = ceil(n / S), and computes, for the G query heads that share kv head g,
+// the chunk's maximum score m, the sum l of exp(score - m) and the
+// unnormalised sum acc of exp(score - m) * v.  With S = 1 it writes
+// acc / l; otherwise it writes (m, l, acc) to the workspace and the CTA that
+// arrives last for (b, g) combines the S chunks in chunk order, rescaling each
+// by exp(m_s - M), and resets the arrival counter.  D threads per CTA; keys
+// are read in batches of 8 per warp with independent loads (the cache reads
+// are latency-bound at decode sizes); softmax and the weighted sum of values
+// run in fp32.
+// ROPE: the CTA first normalises and rotates its G query heads (kept in
+// shared memory); the CTA whose chunk holds position pos also normalises and
+// rotates the kv head's new k row and writes the new k and v rows at pos to
+// the caches, reading the row back after a barrier.  A position outside the
+// cache gives a zero output and writes nothing.
 template <typename T> struct AttnRope {
     const T *k, *v;                    // this step's k / v projections [B, Hkv, D]
     const float *qw, *kw;              // per-head norm weights [D] (may be null)
@@ -223,46 +231,62 @@ template <typename T> struct AttnRope {
     float eps;
 };
 
+struct AttnSplit {
+    int S;                             // CTAs per (b, g)
+    int cmax;                          // score slots per head in shared memory (>= ceil(n / S))
+    float *part;                       // S > 1: [B * Hkv][S][G * D + 2 * G] fp32
+    uint32_t *count;                   // S > 1: [B * Hkv] arrival counters (0 between launches)
+};
+
 template <typename T, int D, int G, bool ROPE>
 __global__ void __launch_bounds__(D) k_attn_decode(const T *q, T *k_cache, T *v_cache,
                                                    const int64_t *pos_dev, int Hq, int Hkv, int64_t L,
-                                                   float scale, T *out, const AttnRope<T> rp) {
+                                                   float scale, T *out, const AttnRope<T> rp,
+                                                   const AttnSplit sp) {
     constexpr int NW = D / 32, E = D / 32, KB = 8;
-    extern __shared__ float sc[];                 // scores [G][L]
+    extern __shared__ float sc[];                 // scores [G][cmax]
     __shared__ float red[G][NW];
     __shared__ float stat[G][2];                  // max, sum
     __shared__ float qs[ROPE ? G : 1][D];         // ROPE: the rotated queries
+    __shared__ int last;
     pdl_launch_dependents();
     pdl_wait();
-    const int bg = blockIdx.x;
+    const int S = sp.S, cmax = sp.cmax;
+    const int bg = blockIdx.x / S, s = blockIdx.x - (blockIdx.x / S) * S;
     const int b = bg / Hkv, g = bg - b * Hkv;
     const int64_t pos = *pos_dev;
     int64_t n = min(pos + 1, L);                       // keys 0..pos (none if pos < 0)
+    if (ROPE && pos >= L) n = 0;
+    const int64_t c = n > 0 ? (n + S - 1) / S : 0;
+    const int64_t j0c = min((int64_t)s * c, n), j1c = min(j0c + c, n);
+    const int64_t nc = j1c - j0c;                       // this chunk's keys
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (ROPE) {
-        if (pos >= L) n = 0;
-        if (n > 0) {
-            // warp w takes heads w, w + NW, ... of the G query heads, k, v; all
-            // its loads (and the position's cos / sin) are issued first
+        if (nc > 0) {
+            // warp w takes heads w, w + NW, ... of the G query heads, and (the
+            // chunk holding pos only) k and v; all its loads (and the
+            // position's cos / sin) are issued first
+            const bool own = pos >= j0c && pos < j1c;
+            const int items = own ? G + 2 : G;
             constexpr int R = (G + 2 + NW - 1) / NW;
             const T *kp = rp.k, *vp = rp.v;
             const float *qw = rp.qw, *kw = rp.kw;
-            float xs[R][E], c[E], sn[E];
+            float xs[R][E], cs[E], sn[E];
 #pragma unroll
             for (int r = 0; r < R; ++r) {
                 const int hh = warp + NW * r;
-                if (hh < G + 2) {
+                if (hh < items) {
                     const T *src = hh < G ? q + ((int64_t)b * Hq + g * G + hh) * D
                                           : (hh == G ? kp : vp) + ((int64_t)b * Hkv + g) * D;
 #pragma unroll
                     for (int e = 0; e < E; ++e) xs[r][e] = ld(src, lane * E + e);
                 }
             }
-            rope_row<T, E>(rp.cosT + pos * D, rp.sinT + pos * D, lane, c, sn);
+            rope_row<T, E>(rp.cosT + pos * D, rp.sinT + pos * D, lane, cs, sn);
 #pragma unroll
             for (int r = 0; r < R; ++r) {
                 const int hh = warp + NW * r;
-                if (hh >= G + 2) break;
+                if (hh >= items) break;
                 if (hh == G + 1) {
                     T *dst = v_cache + (((int64_t)b * Hkv + g) * L + pos) * D;
 #pragma unroll
@@ -270,7 +294,7 @@ __global__ void __launch_bounds__(D) k_attn_decode(const T *q, T *k_cache, T *v_
                     continue;
                 }
                 float o[E];
-                qk_head<T, E>(xs[r], rp.eps, hh < G ? qw : kw, c, sn, lane, o);
+                qk_head<T, E>(xs[r], rp.eps, hh < G ? qw : kw, cs, sn, lane, o);
                 if (hh < G) {
 #pragma unroll
                     for (int e = 0; e < E; ++e) qs[hh][lane * E + e] = o[e];
@@ -295,11 +319,11 @@ __global__ void __launch_bounds__(D) k_attn_decode(const T *q, T *k_cache, T *v_
     float mx[G];
 #pragma unroll
     for (int h = 0; h < G; ++h) mx[h] = -INFINITY;
-    for (int64_t j0 = (int64_t)warp * KB; j0 < n; j0 += (int64_t)NW * KB) {
+    for (int64_t u0 = (int64_t)warp * KB; u0 < nc; u0 += (int64_t)NW * KB) {
         float kv[KB][E];
 #pragma unroll
         for (int u = 0; u < KB; ++u) {                // KB independent row loads
-            const int64_t j = min(j0 + u, n - 1);
+            const int64_t j = j0c + min(u0 + u, nc - 1);
 #pragma unroll
             for (int e = 0; e < E; ++e) kv[u][e] = ld(kb, j * D + lane * E + e);
         }
@@ -311,8 +335,8 @@ __global__ void __launch_bounds__(D) k_attn_decode(const T *q, T *k_cache, T *v_
 #pragma unroll
                 for (int e = 0; e < E; ++e) d += qv[h][e] * kv[u][e];
                 d = warp_sum(d) * scale;
-                if (j0 + u < n) {
-                    if (lane == 0) sc[h * L + j0 + u] = d;
+                if (u0 + u < nc) {
+                    if (lane == 0) sc[h * cmax + u0 + u] = d;
                     mx[h] = fmaxf(mx[h], d);
                 }
             }
@@ -333,9 +357,9 @@ __global__ void __launch_bounds__(D) k_attn_decode(const T *q, T *k_cache, T *v_
     for (int h = 0; h < G; ++h) {
         sum[h] = 0.f;
         const float m = stat[h][0];
-        for (int64_t j = threadIdx.x; j < n; j += D) {
-            const float p = expf(sc[h * L + j] - m);
-            sc[h * L + j] = p;
+        for (int64_t j = threadIdx.x; j < nc; j += D) {
+            const float p = expf(sc[h * cmax + j] - m);
+            sc[h * cmax + j] = p;
             sum[h] += p;
         }
         sum[h] = warp_sum(sum[h]);
@@ -351,31 +375,65 @@ __global__ void __launch_bounds__(D) k_attn_decode(const T *q, T *k_cache, T *v_
         stat[threadIdx.x][1] = t;
     }
     __syncthreads();
-    // out[h][i] = sum_j p_h[j] v[j][i]: thread i, KB independent value loads per step
+    // acc[h][i] = sum_j p_h[j] v[j][i]: thread i, KB independent value loads per step
     const int i = threadIdx.x;
     float acc[G];
 #pragma unroll
     for (int h = 0; h < G; ++h) acc[h] = 0.f;
     int64_t j = 0;
-    for (; j + KB <= n; j += KB) {
+    for (; j + KB <= nc; j += KB) {
         float vv[KB];
 #pragma unroll
-        for (int u = 0; u < KB; ++u) vv[u] = ld(vb, (j + u) * D + i);
+        for (int u = 0; u < KB; ++u) vv[u] = ld(vb, (j0c + j + u) * D + i);
 #pragma unroll
         for (int u = 0; u < KB; ++u)
 #pragma unroll
-            for (int h = 0; h < G; ++h) acc[h] = fmaf(sc[h * L + j + u], vv[u], acc[h]);
+            for (int h = 0; h < G; ++h) acc[h] = fmaf(sc[h * cmax + j + u], vv[u], acc[h]);
     }
-    for (; j < n; ++j) {
-        const float v = ld(vb, j * D + i);
+    for (; j < nc; ++j) {
+        const float v = ld(vb, (j0c + j) * D + i);
 #pragma unroll
-        for (int h = 0; h < G; ++h) acc[h] = fmaf(sc[h * L + j], v, acc[h]);
+        for (int h = 0; h < G; ++h) acc[h] = fmaf(sc[h * cmax + j], v, acc[h]);
     }
+    T *ob = out + ((int64_t)b * Hq + g * G) * D;
+    if (S == 1) {
+#pragma unroll
+        for (int h = 0; h < G; ++h) ob[h * D + i] = from_f32<T>(n > 0 ? acc[h] / stat[h][1] : 0.f);
+        return;
+    }
+    // this chunk's (m, l, acc) -> the workspace; the last CTA of (b, g) combines
+    constexpr int PW = G * D + 2 * G;
+    float *pp = sp.part + ((int64_t)bg * S + s) * PW;
+#pragma unroll
+    for (int h = 0; h < G; ++h) pp[h * D + i] = acc[h];
+    if (i < G) {
+        pp[G * D + i] = nc > 0 ? stat[i][0] : -INFINITY;
+        pp[G * D + G + i] = nc > 0 ? stat[i][1] : 0.f;
+    }
+    __threadfence();                                  // the chunk's values before its arrival
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(sp.count + bg, 1u) == (uint32_t)(S - 1);
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    const float *pb = sp.part + (int64_t)bg * S * PW;
 #pragma unroll
     for (int h = 0; h < G; ++h) {
-        const float tot = stat[h][1];
-        out[((int64_t)b * Hq + g * G + h) * D + i] = from_f32<T>(n > 0 ? acc[h] / tot : 0.f);
+        float M = -INFINITY;
+        for (int t = 0; t < S; ++t) M = fmaxf(M, __ldcg(pb + (int64_t)t * PW + G * D + h));
+        float lsum = 0.f, o = 0.f;
+        if (M > -INFINITY) {
+            for (int t = 0; t < S; ++t) {
+                const float mt = __ldcg(pb + (int64_t)t * PW + G * D + h);
+                if (mt == -INFINITY) continue;
+                const float f = expf(mt - M);
+                lsum = fmaf(__ldcg(pb + (int64_t)t * PW + G * D + G + h), f, lsum);
+                o = fmaf(__ldcg(pb + (int64_t)t * PW + h * D + i), f, o);
+            }
+        }
+        ob[h * D + i] = from_f32<T>(lsum > 0.f ? o / lsum : 0.f);
     }
+    if (threadIdx.x == 0) sp.count[bg] = 0u;          // ready for the next launch
 }
 
 }  // namespace
@@ -459,24 +517,51 @@ extern "C" int cbq_qk_norm_rope(const void *q_dev, const void *k_dev, const void
 
 namespace {
 
+// Splits of the keys per (row, kv head): enough CTAs to cover the SMs about
+// twice, at least 16 keys per split (cache_len bounds the keys), at most 64.
+int attn_splits(int64_t B, int64_t Hkv, int64_t cache_len) {
+    const int64_t target = 2 * (int64_t)cbq_host::sm_count();
+    int64_t S = (target + B * Hkv - 1) / (B * Hkv);
+    S = std::min<int64_t>(S, (cache_len + 15) / 16);
+    S = std::min<int64_t>(S, 64);
+    return (int)std::max<int64_t>(S, 1);
+}
+
+int64_t attn_workspace_bytes(int64_t B, int64_t Hkv, int64_t G, int64_t D, int S) {
+    if (S <= 1) return 0;
+    const int64_t part = B * Hkv * S * (G * D + 2 * G) * 4;
+    return cbq_host::align_up(part, 256) + cbq_host::align_up(B * Hkv * 4, 256);
+}
+
 template <bool ROPE>
 int launch_attn(const void *q_dev, void *k_cache_dev, void *v_cache_dev, int dtype, int64_t B, int64_t Hq,
                 int64_t Hkv, int64_t head_dim, int64_t cache_len, const int64_t *pos_dev, float scale,
                 void *out_dev, const void *k_dev, const void *v_dev, const float *qw, const float *kw,
-                const float *cos_dev, const float *sin_dev, float eps, void *stream) {
+                const float *cos_dev, const float *sin_dev, float eps, void *ws, int64_t ws_bytes,
+                void *stream) {
     if (B < 0 || Hq < 1 || Hkv < 1 || Hq % Hkv || cache_len < 1 || (dtype != CBQ_F32 && dtype != CBQ_BF16))
         return CBQ_ERR_ARG;
     if (head_dim != 64 && head_dim != 128 && head_dim != 256) return CBQ_ERR_UNSUPPORTED;
     const int64_t G = Hq / Hkv;
     if (G < 1 || G > 8) return CBQ_ERR_UNSUPPORTED;
-    const size_t smem = (size_t)cache_len * 4 * (size_t)G;       // scores of the group's heads
-    if (smem > (size_t)cbq_host::max_smem_optin() - 4096 - (ROPE ? (size_t)G * head_dim * 4 : 0))
-        return CBQ_ERR_UNSUPPORTED;
     if (B == 0) return CBQ_OK;
     if (!q_dev || !k_cache_dev || !v_cache_dev || !pos_dev || !out_dev || B * Hkv > 0x7fffffff) return CBQ_ERR_ARG;
     if (ROPE && (!k_dev || !v_dev || !cos_dev || !sin_dev)) return CBQ_ERR_ARG;
+    // keys split over S CTAs when a workspace is given, else one CTA per (row, kv head)
+    int S = ws ? attn_splits(B, Hkv, cache_len) : 1;
+    if (ws && ws_bytes < attn_workspace_bytes(B, Hkv, G, head_dim, S)) return CBQ_ERR_ARG;
+    if (B * Hkv * S > 0x7fffffff) return CBQ_ERR_ARG;
+    AttnSplit sp{S, (int)((cache_len + S - 1) / S), nullptr, nullptr};
+    if (S > 1) {
+        sp.part = static_cast<float *>(ws);
+        sp.count = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(ws) +
+                                                cbq_host::align_up(B * Hkv * S * (G * head_dim + 2 * G) * 4, 256));
+    }
+    const size_t smem = (size_t)sp.cmax * 4 * (size_t)G;       // scores of the group's heads
+    if (smem > (size_t)cbq_host::max_smem_optin() - 4096 - (ROPE ? (size_t)G * head_dim * 4 : 0))
+        return CBQ_ERR_UNSUPPORTED;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const dim3 grid((unsigned)(B * Hkv));
+    const dim3 grid((unsigned)(B * Hkv * S));
 #define CBQ_AT(T, D, GG)                                                                             \
     do {                                                                                             \
         auto kern = k_attn_decode<T, D, GG, ROPE>;                                                   \
@@ -487,7 +572,7 @@ int launch_attn(const void *q_dev, void *k_cache_dev, void *v_cache_dev, int dty
         CBQ_CUDA_TRY(cbq_host::launch_pdl(kern, grid, dim3(D), smem, s, static_cast<const T *>(q_dev), \
                                           static_cast<T *>(k_cache_dev), static_cast<T *>(v_cache_dev), \
                                           pos_dev, (int)Hq, (int)Hkv, cache_len, scale,              \
-                                          static_cast<T *>(out_dev), rp));                           \
+                                          static_cast<T *>(out_dev), rp, sp));                       \
     } while (0)
 #define CBQ_AT_G(T, D)                                                                               \
     do {                                                                                             \
@@ -524,7 +609,7 @@ extern "C" int cbq_attn_decode(const void *q_dev, const void *k_cache_dev, const
     // the kernel only reads the cache in this form
     return launch_attn<false>(q_dev, const_cast<void *>(k_cache_dev), const_cast<void *>(v_cache_dev), dtype, B,
                               Hq, Hkv, head_dim, cache_len, pos_dev, scale, out_dev, nullptr, nullptr, nullptr,
-                              nullptr, nullptr, nullptr, 0.f, stream);
+                              nullptr, nullptr, nullptr, 0.f, nullptr, 0, stream);
 }
 
 extern "C" int cbq_attn_decode_rope(const void *q_dev, const void *k_dev, const void *v_dev, int dtype, int64_t B,
@@ -535,5 +620,34 @@ extern "C" int cbq_attn_decode_rope(const void *q_dev, const void *k_dev, const 
                                     void *stream) {
     return launch_attn<true>(q_dev, k_cache_dev, v_cache_dev, dtype, B, Hq, Hkv, head_dim, cache_len, pos_dev,
                              scale, out_dev, k_dev, v_dev, q_weight_dev, k_weight_dev, cos_dev, sin_dev, eps,
-                             stream);
+                             nullptr, 0, stream);
+}
+
+extern "C" int64_t cbq_attn_workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int64_t head_dim,
+                                            int64_t cache_len) {
+    if (B < 0 || Hq < 1 || Hkv < 1 || Hq % Hkv || head_dim < 1 || cache_len < 1) return -1;
+    return std::max<int64_t>(attn_workspace_bytes(B, Hkv, Hq / Hkv, head_dim, attn_splits(B, Hkv, cache_len)), 256);
+}
+
+extern "C" int cbq_attn_decode_rope_split(const void *q_dev, const void *k_dev, const void *v_dev, int dtype,
+                                          int64_t B, int64_t Hq, int64_t Hkv, int64_t head_dim, float eps,
+                                          const float *q_weight_dev, const float *k_weight_dev,
+                                          const float *cos_dev, const float *sin_dev, const int64_t *pos_dev,
+                                          void *k_cache_dev, void *v_cache_dev, int64_t cache_len, float scale,
+                                          void *out_dev, void *workspace_dev, int64_t workspace_bytes,
+                                          void *stream) {
+    if (!workspace_dev) return CBQ_ERR_ARG;
+    return launch_attn<true>(q_dev, k_cache_dev, v_cache_dev, dtype, B, Hq, Hkv, head_dim, cache_len, pos_dev,
+                             scale, out_dev, k_dev, v_dev, q_weight_dev, k_weight_dev, cos_dev, sin_dev, eps,
+                             workspace_dev, workspace_bytes, stream);
+}
+
+extern "C" int cbq_attn_decode_split(const void *q_dev, const void *k_cache_dev, const void *v_cache_dev,
+                                     int dtype, int64_t B, int64_t Hq, int64_t Hkv, int64_t head_dim,
+                                     int64_t cache_len, const int64_t *pos_dev, float scale, void *out_dev,
+                                     void *workspace_dev, int64_t workspace_bytes, void *stream) {
+    if (!workspace_dev) return CBQ_ERR_ARG;
+    return launch_attn<false>(q_dev, const_cast<void *>(k_cache_dev), const_cast<void *>(v_cache_dev), dtype, B,
+                              Hq, Hkv, head_dim, cache_len, pos_dev, scale, out_dev, nullptr, nullptr, nullptr,
+                              nullptr, nullptr, nullptr, 0.f, workspace_dev, workspace_bytes, stream);
 }

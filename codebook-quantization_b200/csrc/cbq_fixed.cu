@@ -306,12 +306,14 @@ extern "C" int cbq_linear_fixed(const void *x_dev, int x_dtype, int64_t T, int64
                                   static_cast<cudaStream_t>(stream), cbq::kWsCallerZeroed);
 }
 
-extern "C" int cbq_linear_fixed_multi(const void *x_dev, int x_dtype, int64_t T, int64_t ldx, int nmat,
-                                      const uint8_t *const *packed_dev, const int64_t *packed_bytes,
-                                      const int64_t *M, const float *codebook_dev, int64_t C, int bits,
-                                      int64_t K, const float *const *bias_dev, void *const *out_dev,
-                                      const int64_t *ldo, const void *const *resid_dev, int out_dtype,
-                                      int epilogue, void *stream) {
+namespace {
+
+int linear_fixed_multi_impl(const void *x_dev, int x_dtype, int64_t T, int64_t ldx, int nmat,
+                            const uint8_t *const *packed_dev, const int64_t *packed_bytes, const int64_t *M,
+                            const float *codebook_dev, int64_t C, int bits, int64_t K,
+                            const float *const *bias_dev, void *const *out_dev, const int64_t *ldo,
+                            const void *const *resid_dev, int out_dtype, int epilogue, int pn_on,
+                            const float *pn_w, float pn_eps, void *stream) {
     if (nmat < 1 || nmat > kGvMaxMats || !packed_dev || !packed_bytes || !M || !out_dev || !ldo)
         return CBQ_ERR_ARG;
     if (T < 0 || K < 0 || bits < 1 || bits > 16 || C < 1 || C > 65536) return CBQ_ERR_ARG;
@@ -344,8 +346,33 @@ extern "C" int cbq_linear_fixed_multi(const void *x_dev, int x_dtype, int64_t T,
                            resid_dev ? resid_dev[m] : nullptr, ldo[m], (int)M[m]};
     a.out_bf16 = out_dtype == CBQ_BF16;
     a.H = g.H; a.NP = g.NP; a.m128 = 128u; a.m4 = 4u; a.status = nullptr;
+    a.pn_on = pn_on; a.pn_w = pn_w; a.pn_eps = pn_eps;
     return launch_gemv(bits, (int)T, g.nf, x_dtype == CBQ_BF16, a, g.smem, g.grid,
                        static_cast<cudaStream_t>(stream));
+}
+
+}  // namespace
+
+extern "C" int cbq_linear_fixed_multi(const void *x_dev, int x_dtype, int64_t T, int64_t ldx, int nmat,
+                                      const uint8_t *const *packed_dev, const int64_t *packed_bytes,
+                                      const int64_t *M, const float *codebook_dev, int64_t C, int bits,
+                                      int64_t K, const float *const *bias_dev, void *const *out_dev,
+                                      const int64_t *ldo, const void *const *resid_dev, int out_dtype,
+                                      int epilogue, void *stream) {
+    return linear_fixed_multi_impl(x_dev, x_dtype, T, ldx, nmat, packed_dev, packed_bytes, M, codebook_dev, C,
+                                   bits, K, bias_dev, out_dev, ldo, resid_dev, out_dtype, epilogue, 0, nullptr,
+                                   0.f, stream);
+}
+
+extern "C" int cbq_linear_fixed_multi_norm(const void *x_dev, int x_dtype, int64_t T, int64_t ldx, int nmat,
+                                           const uint8_t *const *packed_dev, const int64_t *packed_bytes,
+                                           const int64_t *M, const float *codebook_dev, int64_t C, int bits,
+                                           int64_t K, const float *const *bias_dev, void *const *out_dev,
+                                           const int64_t *ldo, const void *const *resid_dev, int out_dtype,
+                                           int epilogue, const float *norm_weight_dev, float eps, void *stream) {
+    return linear_fixed_multi_impl(x_dev, x_dtype, T, ldx, nmat, packed_dev, packed_bytes, M, codebook_dev, C,
+                                   bits, K, bias_dev, out_dev, ldo, resid_dev, out_dtype, epilogue, 1,
+                                   norm_weight_dev, eps, stream);
 }
 
 namespace {

@@ -30,6 +30,8 @@
 //     overlaps the table fill, and with programmatic dependent launch both
 //     happen while the previous kernel on the stream is still finishing.
 #pragma once
+#include <type_traits>
+
 #include "cbq_common.cuh"
 
 namespace cbq {
@@ -125,6 +127,13 @@ struct GemvArgs {
     uint32_t *status;
     GemvPeers peers;     // kEpiPeer only
     GemvNorm norm;
+    // RMSNorm of the activations on load (the norm that precedes the linear
+    // layer): every CTA reduces the sum of squares of each token row of x over
+    // K in the same order, then x[k] -> round(w[k] * round(x[k] * rsqrt(
+    // mean(x^2) + eps))) (HF Qwen3RMSNorm; round = the activation dtype).
+    int pn_on;
+    const float *pn_w;   // [K] or null (unit weights)
+    float pn_eps;
 };
 
 // The norm of GemvNorm, run by the last CTA (all its threads).  red: 16
@@ -358,6 +367,49 @@ __device__ __forceinline__ void gv_load_x(const __nv_bfloat16 *xr, int k0, int K
     }
 }
 
+// The activation pre-norm of GemvArgs: scale[t] = rsqrt(mean(x[t]^2) + eps)
+// for the launch's tokens, every CTA the same value (thread i adds elements
+// i, i + blockDim, ... in order, then a fixed tree).  All threads call it.
+template <typename XT, int TB>
+__device__ __forceinline__ void gv_prenorm_scales(const GemvArgs &a, float (&scale)[TB], float *red) {
+    const XT *x = static_cast<const XT *>(a.x);
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    for (int t = 0; t < TB; ++t) {
+        float ss = 0.f;
+        if (t < a.ntok) {
+            const XT *xr = x + (a.t0 + t) * a.ldx;
+            for (int k = tid; k < a.K; k += kGvWarps * 32) {
+                const float v = to_f32<XT>(xr[k]);
+                ss = fmaf(v, v, ss);
+            }
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) red[w] = ss;
+        __syncthreads();
+        float tot = 0.f;
+#pragma unroll
+        for (int i = 0; i < kGvWarps; ++i) tot += red[i];
+        scale[t] = rsqrtf(tot / (float)a.K + a.pn_eps);
+        __syncthreads();                                   // red[] reuse
+    }
+}
+
+// Normalise NF loaded activations starting at k0 (see gv_prenorm_scales).
+template <typename XT, int NF>
+__device__ __forceinline__ void gv_prenorm_apply(float (&v)[NF], float scale, const float *w, int k0, int K) {
+    if (k0 >= K) return;
+    auto rnd = [](float f) {
+        if constexpr (std::is_same<XT, float>::value) return f;
+        else return __bfloat162float(__float2bfloat16_rn(f));
+    };
+#pragma unroll
+    for (int i = 0; i < NF; ++i) {
+        float y = rnd(v[i] * scale);
+        if (w) y = rnd(__ldg(w + k0 + i) * y);
+        v[i] = y;
+    }
+}
+
 template <int BITS, int TB, int NF, typename XT>
 __global__ void __launch_bounds__(kGvWarps * 32, 1) k_gemv_fixed(const GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -450,6 +502,13 @@ __global__ void __launch_bounds__(kGvWarps * 32, 1) k_gemv_fixed(const GemvArgs 
     // Weights and codebook are constant; the activations (and the residual
     // the epilogue reads) come from the previous kernel.
     pdl_wait();
+    float pn_scale[TB];
+#pragma unroll
+    for (int t = 0; t < TB; ++t) pn_scale[t] = 1.f;
+    if (a.pn_on) {
+        __shared__ float pn_red[kGvWarps];
+        gv_prenorm_scales<XT, TB>(a, pn_scale, pn_red);
+    }
 
     const uint32_t cb_base = smem_u32(cbs);
     const uint32_t head_off = cb_base + (uint32_t)lane * 4u;
@@ -476,8 +535,10 @@ __global__ void __launch_bounds__(kGvWarps * 32, 1) k_gemv_fixed(const GemvArgs 
             const int k0 = s * kGvSeg + lane * NF;
 #pragma unroll
             for (int t = 0; t < TB; ++t) {
-                if (t < a.ntok) gv_load_x<NF>(x + (a.t0 + t) * a.ldx, k0, K, xr[t]);
-                else {
+                if (t < a.ntok) {
+                    gv_load_x<NF>(x + (a.t0 + t) * a.ldx, k0, K, xr[t]);
+                    if (a.pn_on) gv_prenorm_apply<XT, NF>(xr[t], pn_scale[t], a.pn_w, k0, K);
+                } else {
 #pragma unroll
                     for (int q = 0; q < NF; ++q) xr[t][q] = 0.f;
                 }

@@ -157,14 +157,16 @@ class GPUAcceleratedLinear:
         return res if res.dtype == want else res.to(want)
 
 
-def linear_fixed_multi(mats, x: torch.Tensor, outs, epilogue: int = 0, resids=None) -> bool:
+def linear_fixed_multi(mats, x: torch.Tensor, outs, epilogue: int = 0, resids=None, norm=None) -> bool:
     """One launch of ``cbq_linear_fixed_multi`` over ``mats`` (GPUAcceleratedLinear
     objects sharing K, bits and codebook) for ``x [T, K]``.  ``outs[i]`` are
     ``[T, M_i]`` tensors (for ``CBQ_EPI_SILU_MUL`` only ``outs[0]`` is
     written); ``resids[i]`` the residual inputs of ``CBQ_EPI_RESIDUAL`` (may be
-    ``outs[i]`` itself).  Returns False, having launched nothing, when the
-    shape is outside what the fused kernel supports (T > 2, unaligned rows);
-    the caller then runs the matrices one by one."""
+    ``outs[i]`` itself).  ``norm=(weight or None, eps)``: ``x`` is the
+    un-normalised residual stream and the launch applies the RMSNorm as it
+    loads it (``cbq_linear_fixed_multi_norm``).  Returns False, having
+    launched nothing, when the shape is outside what the fused kernel supports
+    (T > 2, unaligned rows); the caller then runs the matrices one by one."""
     import ctypes as ct
     n = len(mats)
     m0 = mats[0]
@@ -187,14 +189,20 @@ def linear_fixed_multi(mats, x: torch.Tensor, outs, epilogue: int = 0, resids=No
     optrs = (P * n)(*[o.data_ptr() for o in outs])
     ldo = (I64 * n)(*[o.stride(0) if o.dim() > 1 and T > 1 else o.shape[-1] for o in outs])
     rp = None if resids is None else (P * n)(*[r.data_ptr() for r in resids])
-    rc = _lib.lib().cbq_linear_fixed_multi(
-        x2.data_ptr(), xcode, T, x2.stride(0) if T > 1 else m0.K, n, packed, nbytes, Ms,
-        m0.codebook.data_ptr(), m0.C, m0.bits, m0.K, None, optrs, ldo, rp, ocode, int(epilogue),
-        device_stream(m0.device))
+    common = (x2.data_ptr(), xcode, T, x2.stride(0) if T > 1 else m0.K, n, packed, nbytes, Ms,
+              m0.codebook.data_ptr(), m0.C, m0.bits, m0.K, None, optrs, ldo, rp, ocode, int(epilogue))
+    if norm is None:
+        fn = "cbq_linear_fixed_multi"
+        rc = _lib.lib().cbq_linear_fixed_multi(*common, device_stream(m0.device))
+    else:
+        fn = "cbq_linear_fixed_multi_norm"
+        w, eps = norm
+        rc = _lib.lib().cbq_linear_fixed_multi_norm(*common, None if w is None else w.data_ptr(), float(eps),
+                                                    device_stream(m0.device))
     if rc == _lib.CBQ_ERR_UNSUPPORTED:
         return False
     if rc != _lib.CBQ_OK:
-        raise _lib.CbqError("cbq_linear_fixed_multi", rc)
+        raise _lib.CbqError(fn, rc)
     return True
 
 

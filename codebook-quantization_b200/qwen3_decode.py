@@ -134,7 +134,7 @@ def _rms(x, eps):
 class Qwen3Decoder:
     def __init__(self, weights: CompressedQwen3Weights, batch: int, max_len: int,
                  act_dtype=torch.bfloat16, group: Optional[dist.ProcessGroup] = None, fused: bool = True,
-                 allreduce: str = "peer", fuse_norm: bool = False, fuse_rope: bool = True):
+                 allreduce: str = "peer", fuse_norm: bool = False, fuse_rope: bool = True, prenorm: bool = True):
         self.w, self.cfg = weights, weights.cfg
         cfg = self.cfg
         self.dev = weights.device
@@ -164,6 +164,11 @@ class Qwen3Decoder:
         # before it (measured slower on a B200 than its own one-CTA launch,
         # which waits on the SM the GEMV grid leaves free; off by default)
         self.fuse_norm, self.fuse_rope = fuse_norm, fuse_rope
+        # one GPU, fixed-width streams, batch <= 2: each RMSNorm runs inside the
+        # GEMV that consumes it (the norm applied as the residual stream is
+        # loaded; cbq_linear_fixed_multi_norm), so a layer is five launches
+        self.prenorm = (fused and prenorm and not fuse_norm and weights.world == 1 and not weights.huffman
+                        and batch <= 2)
         if fused:
             hq, hkv = self.hl * d, self.kvl * d
             z = lambda n: torch.zeros(batch, n, dtype=act_dtype, device=self.dev)
@@ -171,9 +176,13 @@ class Qwen3Decoder:
             self.q, self.k, self.v = z(hq), z(hkv), z(hkv)
             self.a, self.qn = z(hq), (None if fuse_rope else z(hq))
             self.m = z(cfg.inter // self.world)
+            self.logits_buf = z(cfg.vocab // self.world)
             self.code = _lib.CBQ_BF16 if act_dtype == torch.bfloat16 else _lib.CBQ_F32
             # arrival count of the GEMVs whose last CTA normalises (0 between launches)
             self.arrive = torch.zeros(1, dtype=torch.int32, device=self.dev)
+            # split-key attention: partial softmax states + arrival counters (0 between launches)
+            n = _lib.query("cbq_attn_workspace_bytes", batch, self.hl, self.kvl, d, max_len)
+            self.attn_ws = torch.zeros(n, dtype=torch.uint8, device=self.dev)
         self.peer = None
         if fused and self.world > 1 and allreduce == "peer" and not weights.huffman and batch <= 2:
             self.peer = _PeerAllReduce(self, 2 * cfg.layers)
@@ -256,28 +265,41 @@ class Qwen3Decoder:
             for m, o in zip(mats, outs):
                 m(x, out=o)
 
+    def _linear_normed(self, mats, outs, epilogue=_lib.CBQ_EPI_STORE):
+        """RMSNorm(self.x) @ W^T for ``mats``: the norm inside the GEMV launch
+        when ``prenorm`` is on and the shape is supported, else cbq_rmsnorm
+        into self.h followed by the GEMV."""
+        if self.prenorm and linear_fixed_multi(mats, self.x, outs, epilogue, norm=(None, self.cfg.rms_eps)):
+            return
+        self._rmsnorm(self.x, self.h)
+        self._linear(mats, outs, epilogue)
+
     def _step_fused(self):
         cfg, B, d, dt = self.cfg, self.B, self.cfg.head_dim, self.dt
         stream = device_stream(self.dev)
         if self.peer is not None:
             self.peer.epoch.add_(1)
         self.emb(self.ids, out=self.x)
+        if self.prenorm:
+            return self._step_prenorm()
         self._rmsnorm(self.x, self.h)
         for li, (q_p, k_p, v_p, o_p, g_p, u_p, d_p) in enumerate(self.layer_mods):
             self._linear((q_p, k_p, v_p), (self.q, self.k, self.v))
+            ws, nws = self.attn_ws.data_ptr(), self.attn_ws.numel()
             if self.fuse_rope:
-                _lib.call("cbq_attn_decode_rope", self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(),
+                _lib.call("cbq_attn_decode_rope_split", self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(),
                           self.code, B, self.hl, self.kvl, d, float(cfg.rms_eps), None, None, self.cos.data_ptr(),
                           self.sin.data_ptr(), self.pos.data_ptr(), self.k_cache[li].data_ptr(),
-                          self.v_cache[li].data_ptr(), self.max_len, float(d ** -0.5), self.a.data_ptr(), stream)
+                          self.v_cache[li].data_ptr(), self.max_len, float(d ** -0.5), self.a.data_ptr(), ws, nws,
+                          stream)
             else:
                 _lib.call("cbq_qk_norm_rope", self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(), self.code,
                           B, self.hl, self.kvl, d, float(cfg.rms_eps), None, None, self.cos.data_ptr(),
                           self.sin.data_ptr(), self.pos.data_ptr(), self.qn.data_ptr(),
                           self.k_cache[li].data_ptr(), self.v_cache[li].data_ptr(), self.max_len, stream)
-                _lib.call("cbq_attn_decode", self.qn.data_ptr(), self.k_cache[li].data_ptr(),
+                _lib.call("cbq_attn_decode_split", self.qn.data_ptr(), self.k_cache[li].data_ptr(),
                           self.v_cache[li].data_ptr(), self.code, B, self.hl, self.kvl, d, self.max_len,
-                          self.pos.data_ptr(), float(d ** -0.5), self.a.data_ptr(), stream)
+                          self.pos.data_ptr(), float(d ** -0.5), self.a.data_ptr(), ws, nws, stream)
             if self.world == 1:
                 self._residual_norm(o_p, self.a)
             elif self.peer is not None:
@@ -296,6 +318,30 @@ class Qwen3Decoder:
                 self._allreduce(self.y)
                 self._rmsnorm(self.x, self.h, add=self.y)
         self._finish(self.lm_head(self.h))
+
+    def _step_prenorm(self):
+        """One GPU: five launches per layer (q/k/v with the input norm,
+        attention, o with the residual add, gate/up with the post-attention
+        norm, down with the residual add); the final norm runs in lm_head."""
+        cfg, B, d = self.cfg, self.B, self.cfg.head_dim
+        stream = device_stream(self.dev)
+        ws, nws = self.attn_ws.data_ptr(), self.attn_ws.numel()
+        for li, (q_p, k_p, v_p, o_p, g_p, u_p, d_p) in enumerate(self.layer_mods):
+            self._linear_normed((q_p, k_p, v_p), (self.q, self.k, self.v))
+            _lib.call("cbq_attn_decode_rope_split", self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(),
+                      self.code, B, self.hl, self.kvl, d, float(cfg.rms_eps), None, None, self.cos.data_ptr(),
+                      self.sin.data_ptr(), self.pos.data_ptr(), self.k_cache[li].data_ptr(),
+                      self.v_cache[li].data_ptr(), self.max_len, float(d ** -0.5), self.a.data_ptr(), ws, nws,
+                      stream)
+            self._linear((o_p,), (self.x,), _lib.CBQ_EPI_RESIDUAL, (self.x,), x=self.a)
+            self._linear_normed((g_p, u_p), (self.m,), _lib.CBQ_EPI_SILU_MUL)
+            self._linear((d_p,), (self.x,), _lib.CBQ_EPI_RESIDUAL, (self.x,), x=self.m)
+        if isinstance(self.lm_head, GPUAcceleratedLinear):
+            self._linear_normed((self.lm_head,), (self.logits_buf,))
+            self._finish(self.logits_buf)
+        else:
+            self._rmsnorm(self.x, self.h)
+            self._finish(self.lm_head(self.h))
 
     def _finish(self, logits):
         self.logits = logits
@@ -316,6 +362,8 @@ class Qwen3Decoder:
         if not self.fused:
             return 1 + 7 * n + 1          # embedding, 7 linears per layer, lm_head
         attn = 1 if self.fuse_rope else 2
+        if self.prenorm:                  # embedding, 5 per layer (norms inside the GEMVs), lm_head
+            return 1 + 5 * n + 1
         if self.w.huffman or self.B > 2:  # one launch per linear, separate RMSNorms
             per = 3 + attn + 1 + 2 + 1 + 2
         elif (self.world == 1 or self.peer is not None) and self.fuse_norm:

@@ -130,6 +130,21 @@ int cbq_linear_fixed_multi(const void *x_dev, int x_dtype, int64_t T, int64_t ld
                            const int64_t *ldo, const void *const *resid_dev, int out_dtype,
                            int epilogue, void *stream);
 
+/* cbq_linear_fixed_multi with the RMSNorm that precedes the linear layers
+ * applied to the activations as they are loaded: x is the un-normalised
+ * residual stream, and every CTA computes rsqrt(mean(x[t]^2) + eps) of each
+ * token row over K itself, then uses round(w[k] * round(x[t,k] * scale))
+ * (HF Qwen3RMSNorm; round = the activation dtype; norm_weight_dev fp32 [K]
+ * or NULL for unit weights).  One launch replaces a norm launch and the
+ * GEMV.  Same support rules as cbq_linear_fixed_multi (T <= 2, else
+ * CBQ_ERR_UNSUPPORTED before launching).  No counterpart in the reference. */
+int cbq_linear_fixed_multi_norm(const void *x_dev, int x_dtype, int64_t T, int64_t ldx, int nmat,
+                                const uint8_t *const *packed_dev, const int64_t *packed_bytes, const int64_t *M,
+                                const float *codebook_dev, int64_t C, int bits, int64_t K,
+                                const float *const *bias_dev, void *const *out_dev, const int64_t *ldo,
+                                const void *const *resid_dev, int out_dtype, int epilogue,
+                                const float *norm_weight_dev, float eps, void *stream);
+
 /* Tensor-parallel row-parallel layer (o_proj, down_proj), fused with the
  * data movement of its all-reduce: the GEMV of this rank's K-block writes its
  * partial product [T, M] into every rank's slot for this rank
@@ -382,6 +397,32 @@ int cbq_attn_decode_rope(const void *q_dev, const void *k_dev, const void *v_dev
                          const float *k_weight_dev, const float *cos_dev, const float *sin_dev,
                          const int64_t *pos_dev, void *k_cache_dev, void *v_cache_dev, int64_t cache_len,
                          float scale, void *out_dev, void *stream);
+
+/* Workspace bytes of the split-key attention entry points below for this
+ * shape (its arrival counters must be zero before the first call; every call
+ * leaves them zero).  No counterpart in the reference. */
+int64_t cbq_attn_workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int64_t head_dim, int64_t cache_len);
+
+/* cbq_attn_decode_rope / cbq_attn_decode with the keys of every (row, kv
+ * head) split over several CTAs (flash-decoding): each CTA attends over one
+ * chunk of the keys and writes its partial softmax state (max, sum,
+ * unnormalised weighted values) to the workspace, and the CTA that finishes
+ * a (row, kv head) last combines the chunks in chunk order.  The number of
+ * chunks depends only on B, Hkv, cache_len and the SM count, so a call is
+ * deterministic.  Results equal the one-CTA forms up to the fp32 summation
+ * order.  workspace_bytes >= cbq_attn_workspace_bytes(...), else CBQ_ERR_ARG.
+ * Calls that share a workspace must not overlap on the GPU.  No counterpart
+ * in the reference (HF attention on the host framework's side). */
+int cbq_attn_decode_rope_split(const void *q_dev, const void *k_dev, const void *v_dev, int dtype, int64_t B,
+                               int64_t Hq, int64_t Hkv, int64_t head_dim, float eps, const float *q_weight_dev,
+                               const float *k_weight_dev, const float *cos_dev, const float *sin_dev,
+                               const int64_t *pos_dev, void *k_cache_dev, void *v_cache_dev, int64_t cache_len,
+                               float scale, void *out_dev, void *workspace_dev, int64_t workspace_bytes,
+                               void *stream);
+int cbq_attn_decode_split(const void *q_dev, const void *k_cache_dev, const void *v_cache_dev, int dtype,
+                          int64_t B, int64_t Hq, int64_t Hkv, int64_t head_dim, int64_t cache_len,
+                          const int64_t *pos_dev, float scale, void *out_dev, void *workspace_dev,
+                          int64_t workspace_bytes, void *stream);
 
 #ifdef __cplusplus
 }

@@ -36,6 +36,37 @@ def _mats(dev, Ms, K, bits=13, seed=0):
 
 @pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
 @pytest.mark.parametrize("T", [1, 2])
+@pytest.mark.parametrize("epi,Ms,K", [(0, [4096, 1024, 1024], 4096), (2, [3072, 3072], 2048), (0, [151936], 256)],
+                         ids=["qkv", "gate-up", "lm-head"])
+@pytest.mark.parametrize("weighted", [False, True], ids=["unit", "weight"])
+def test_multi_norm_matches_rmsnorm_then_gemv(dt, T, epi, Ms, K, weighted):
+    """cbq_linear_fixed_multi_norm (RMSNorm applied while the GEMV loads the
+    residual stream) against cbq_rmsnorm followed by cbq_linear_fixed_multi:
+    the same roundings, only the sum-of-squares order differs (fp32: rel-L2
+    1e-5; bf16: a rare last-bit flip of a normalised activation, 1e-2)."""
+    dev = need_cuda()
+    mats = _mats(dev, Ms, K, seed=len(Ms) + K)
+    x = (torch.randn(T, K, device=dev) * 3).to(dt)
+    w = (torch.rand(K, device=dev) + 0.5) if weighted else None
+    code = L.CBQ_BF16 if dt == torch.bfloat16 else L.CBQ_F32
+    h = torch.empty_like(x)
+    L.call("cbq_rmsnorm", x.data_ptr(), None, code, T, K, None if w is None else w.data_ptr(), 1e-6, h.data_ptr(),
+           torch.cuda.current_stream(dev).cuda_stream)
+    n_out = 1 if epi == L.CBQ_EPI_SILU_MUL else len(Ms)
+    ref = [torch.empty(T, Ms[i], device=dev, dtype=dt) for i in range(n_out)]
+    got = [torch.empty_like(r) for r in ref]
+    assert G.linear_fixed_multi(mats, h, ref, epi)
+    x0 = x.clone()
+    assert G.linear_fixed_multi(mats, x, got, epi, norm=(w, 1e-6))
+    torch.cuda.synchronize()
+    assert torch.equal(x, x0)                              # the residual stream is only read
+    tol = 1e-5 if dt == torch.float32 else 1e-2
+    for r, g in zip(ref, got):
+        assert rel_l2(g.float().cpu().numpy(), r.float().cpu().numpy()) < tol
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+@pytest.mark.parametrize("T", [1, 2])
 def test_multi_store_matches_single_calls(dt, T):
     dev = need_cuda()
     mats = _mats(dev, [512, 128, 128], 1024)
@@ -209,6 +240,86 @@ def test_attn_decode_rope_equals_the_two_launches(dt, d, G, pos):
     L.call("cbq_attn_decode_rope", q.data_ptr(), k.data_ptr(), v.data_ptr(), code, B, Hq, Hkv, d, 1e-6,
            qw.data_ptr(), kw.data_ptr(), cos.data_ptr(), sin.data_ptr(), p.data_ptr(), kc3.data_ptr(),
            vc3.data_ptr(), Lc, d ** -0.5, out.data_ptr(), st)
+    torch.cuda.synchronize()
+    assert torch.equal(kc3, kc0) and torch.equal(vc3, vc0)
+    assert not bool(out.any())
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+@pytest.mark.parametrize("B,Hq,Hkv,d,Lc,pos", [(1, 32, 8, 128, 200, 171), (2, 8, 2, 128, 512, 77),
+                                               (1, 4, 1, 128, 200, 0), (8, 32, 8, 128, 200, 150),
+                                               (2, 12, 4, 64, 400, 399), (1, 16, 2, 256, 64, 35)])
+def test_attn_decode_split_matches_sdpa(dt, B, Hq, Hkv, d, Lc, pos):
+    """Split-key attention (flash-decoding: chunks of the keys on separate
+    CTAs, the last CTA combines) against the fp32 softmax reference, on two
+    calls in a row (the arrival counters are reused)."""
+    dev = need_cuda()
+    q = torch.randn(B, Hq, d, device=dev).to(dt)
+    kc = torch.randn(B, Hkv, Lc, d, device=dev).to(dt)
+    vc = torch.randn(B, Hkv, Lc, d, device=dev).to(dt)
+    p = torch.tensor([pos], device=dev)
+    code = L.CBQ_BF16 if dt == torch.bfloat16 else L.CBQ_F32
+    nws = L.query("cbq_attn_workspace_bytes", B, Hq, Hkv, d, Lc)
+    ws = torch.zeros(nws, dtype=torch.uint8, device=dev)
+    kr = kc[:, :, :pos + 1].float().repeat_interleave(Hq // Hkv, dim=1)
+    vr = vc[:, :, :pos + 1].float().repeat_interleave(Hq // Hkv, dim=1)
+    att = torch.softmax((q.float().unsqueeze(2) @ kr.transpose(-1, -2)) * d ** -0.5, dim=-1)
+    ref = (att @ vr).reshape(B, Hq * d)
+    tol = 1e-5 if dt == torch.float32 else 8e-3
+    outs = []
+    for _ in range(2):
+        out = torch.full((B, Hq * d), float("nan"), device=dev).to(dt)
+        L.call("cbq_attn_decode_split", q.data_ptr(), kc.data_ptr(), vc.data_ptr(), code, B, Hq, Hkv, d, Lc,
+               p.data_ptr(), d ** -0.5, out.data_ptr(), ws.data_ptr(), nws, torch.cuda.current_stream(dev).cuda_stream)
+        torch.cuda.synchronize()
+        assert rel_l2(out.float().cpu().numpy(), ref.cpu().numpy()) < tol
+        outs.append(out)
+    assert torch.equal(outs[0], outs[1])                    # deterministic combine order
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+@pytest.mark.parametrize("d,G,pos", [(128, 4, 0), (128, 4, 157), (64, 3, 140), (128, 8, 9)])
+def test_attn_decode_rope_split_matches_one_cta(dt, d, G, pos):
+    """The split form of the fused rope + attention launch writes the same
+    cache rows as the one-CTA form, bit for bit, and the same output within
+    the fp32 summation-order tolerance; a position outside the cache writes
+    nothing and gives 0."""
+    dev = need_cuda()
+    qd = importlib.import_module("codebook-quantization_b200.qwen3_decode")
+    B, Hkv, Lc = 2, 2, 160
+    Hq = G * Hkv
+    cos, sin = qd.rope_tables(d, Lc, 1e6, dev)
+    q = torch.randn(B, Hq * d, device=dev).to(dt)
+    k = torch.randn(B, Hkv * d, device=dev).to(dt)
+    v = torch.randn(B, Hkv * d, device=dev).to(dt)
+    qw = torch.rand(d, device=dev) + 0.5
+    kw = torch.rand(d, device=dev) + 0.5
+    kc0 = torch.randn(B, Hkv, Lc, d, device=dev).to(dt)
+    vc0 = torch.randn(B, Hkv, Lc, d, device=dev).to(dt)
+    p = torch.tensor([pos], device=dev)
+    code = L.CBQ_BF16 if dt == torch.bfloat16 else L.CBQ_F32
+    st = torch.cuda.current_stream(dev).cuda_stream
+    nws = L.query("cbq_attn_workspace_bytes", B, Hq, Hkv, d, Lc)
+    ws = torch.zeros(nws, dtype=torch.uint8, device=dev)
+    kc1, vc1 = kc0.clone(), vc0.clone()
+    ref = torch.empty(B, Hq * d, device=dev, dtype=dt)
+    L.call("cbq_attn_decode_rope", q.data_ptr(), k.data_ptr(), v.data_ptr(), code, B, Hq, Hkv, d, 1e-6,
+           qw.data_ptr(), kw.data_ptr(), cos.data_ptr(), sin.data_ptr(), p.data_ptr(), kc1.data_ptr(),
+           vc1.data_ptr(), Lc, d ** -0.5, ref.data_ptr(), st)
+    kc2, vc2 = kc0.clone(), vc0.clone()
+    out = torch.empty_like(ref)
+    L.call("cbq_attn_decode_rope_split", q.data_ptr(), k.data_ptr(), v.data_ptr(), code, B, Hq, Hkv, d, 1e-6,
+           qw.data_ptr(), kw.data_ptr(), cos.data_ptr(), sin.data_ptr(), p.data_ptr(), kc2.data_ptr(),
+           vc2.data_ptr(), Lc, d ** -0.5, out.data_ptr(), ws.data_ptr(), nws, st)
+    torch.cuda.synchronize()
+    assert torch.equal(kc2, kc1) and torch.equal(vc2, vc1)
+    tol = 1e-6 if dt == torch.float32 else 8e-3
+    assert rel_l2(out.float().cpu().numpy(), ref.float().cpu().numpy()) < tol
+    p.fill_(Lc)
+    kc3, vc3 = kc0.clone(), vc0.clone()
+    L.call("cbq_attn_decode_rope_split", q.data_ptr(), k.data_ptr(), v.data_ptr(), code, B, Hq, Hkv, d, 1e-6,
+           qw.data_ptr(), kw.data_ptr(), cos.data_ptr(), sin.data_ptr(), p.data_ptr(), kc3.data_ptr(),
+           vc3.data_ptr(), Lc, d ** -0.5, out.data_ptr(), ws.data_ptr(), nws, st)
     torch.cuda.synchronize()
     assert torch.equal(kc3, kc0) and torch.equal(vc3, vc0)
     assert not bool(out.any())
