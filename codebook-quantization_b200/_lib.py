@@ -46,6 +46,7 @@ SIGNATURES = {
     "cbq_linear_fixed_noalloc": (_INT, [_P, _INT, _I64, _I64, _P, _I64, _P, _I64, _INT, _I64, _I64, _P,
                                         _P, _INT, _I64, _P]),
     "cbq_embedding_fixed": (_INT, [_P, _I64, _P, _I64, _P, _I64, _INT, _I64, _I64, _P, _INT, _P, _P]),
+    "cbq_unpack_fixed": (_INT, [_P, _I64, _INT, _I64, _P, _P]),
     "cbq_pack_fixed": (_INT, [_P, _I64, _INT, _P, _I64, _P]),
     "cbq_huff_tables_bytes": (_I64, [_I64]),
     "cbq_huff_tables_build": (_INT, [_P, _I64, _P, _I64]),

@@ -80,6 +80,19 @@ __global__ void k_embedding_fixed(const int64_t *ids, const uint8_t *packed, con
     }
 }
 
+// idx[i] = field i of an LSB-first b-bit stream (the 4-byte window read of
+// src/compressed_matmul.c:334-347); grid-stride.
+__global__ void k_unpack_fixed(const uint8_t *packed, int bits, int64_t n, uint16_t *out) {
+    const uint32_t mask = (1u << bits) - 1u;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t bit = i * bits;
+        const uint8_t *p = packed + (bit >> 3);
+        const uint32_t win = (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) |
+                             ((uint32_t)p[3] << 24);
+        out[i] = (uint16_t)((win >> (bit & 7)) & mask);
+    }
+}
+
 // One thread per output 32-bit word: OR in every field that overlaps it.
 __global__ void k_pack_fixed(const uint16_t *idx, int64_t n, int bits, uint32_t *out,
                              int64_t nwords) {
@@ -501,6 +514,18 @@ extern "C" int cbq_embedding_fixed(const int64_t *ids_dev, int64_t T, const uint
         k_embedding_fixed<__nv_bfloat16><<<grid, 256, 0, s>>>(
             ids_dev, packed_dev, codebook_dev, (int)C, bits, vocab, H,
             static_cast<__nv_bfloat16 *>(out_dev), status_dev);
+    CBQ_CUDA_TRY(cudaGetLastError());
+    return CBQ_OK;
+}
+
+extern "C" int cbq_unpack_fixed(const uint8_t *packed_dev, int64_t packed_bytes, int bits, int64_t n,
+                                uint16_t *idx_dev, void *stream) {
+    if (n < 0 || bits < 1 || bits > 16) return CBQ_ERR_ARG;
+    if (n == 0) return CBQ_OK;
+    if (!packed_dev || !idx_dev || packed_bytes < cbq_fixed_stream_bytes(1, n, bits)) return CBQ_ERR_ARG;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int64_t blocks = std::min<int64_t>((n + 255) / 256, (int64_t)cbq_host::sm_count() * 16);
+    k_unpack_fixed<<<(unsigned)blocks, 256, 0, s>>>(packed_dev, bits, n, idx_dev);
     CBQ_CUDA_TRY(cudaGetLastError());
     return CBQ_OK;
 }

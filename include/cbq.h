@@ -231,6 +231,12 @@ int cbq_embedding_fixed(const int64_t *ids_dev, int64_t T,
                         int64_t vocab, int64_t H, void *out_dev, int out_dtype,
                         uint32_t *status_dev, void *stream);
 
+/* idx[i] = field i (i < n) of a b-bit LSB-first stream on the device (the
+ * inverse of cbq_pack_fixed; the reference's unpack_any_bits,
+ * src/bitpack.py:97-156).  packed_bytes >= cbq_fixed_stream_bytes(1, n, bits). */
+int cbq_unpack_fixed(const uint8_t *packed_dev, int64_t packed_bytes, int bits, int64_t n, uint16_t *idx_dev,
+                     void *stream);
+
 /* Write the LSB-first stream of n indices (the device twin of
  * pack_any_bits, src/bitpack.py:32-94).  out_bytes >= ceil(n*bits/8) rounded
  * up to 4; bytes past ceil(n*bits/8) are written as zero. */

@@ -64,3 +64,15 @@ def test_direct_codebook_without_cuda_raises():
         cbq.AdaptiveCodebookLinear.from_compressed("x", d, {})
     with pytest.raises(RuntimeError):
         cbq.GPUAcceleratedLinear("x", d["indices"], d["codebook"], (8, 128), d["bits"])
+
+
+def test_model_dir_config_and_layout(tmp_path):
+    """The HF config.json of a compressed model directory maps onto the
+    decoder shape, and the cache directory names follow the reference's."""
+    import json
+    md = cbq.model_dir
+    cfg = cbq.qwen3.QWEN3_8B
+    (tmp_path / "config.json").write_text(json.dumps(md._config_json(cfg)))
+    assert md.read_qwen3_config(tmp_path) == cfg
+    assert md.cache_dir_for(tmp_path, False).name == "codebook-lossless"
+    assert md.cache_dir_for(tmp_path, True).name == "codebook-lossless-huffman"
