@@ -478,6 +478,7 @@ def decode_run(W, batch, steps, warmup, world, group, dev, local, allreduce="pee
                 ids_host.copy_(next_host)
             res["ms_e2e"] = timed_ms(torch, dist, e2e_step, steps, world, dev) / steps
     res["launches_per_step"] = dec.launches_per_step()
+    res["layer_launches"] = dec.layer_launches()
     res["peer"] = dec.peer is not None
     res["fuse_norm"], res["fuse_rope"] = dec.fuse_norm, dec.fuse_rope
     res["max_len"] = max_len
@@ -710,9 +711,7 @@ def main():
                        "timed_positions": r["positions"],
                        "allreduce": ("peer-memory (GEMV epilogue + RMSNorm)" if r["peer"]
                                      else ("nccl" if world > 1 else "none")),
-                       "launches_per_layer": ("q/k/v, attention" + ("" if r["fuse_rope"] else " (+ q/k norm rope)")
-                                              + ", o" + (" + norm" if r["fuse_norm"] else ", norm")
-                                              + ", gate/up, down" + (" + norm" if r["fuse_norm"] else ", norm")),
+                       "launches_per_layer": r["layer_launches"],
                        "l2": "weights 12.3 GB >> 126 MB L2 (no flush)",
                        "stream_bytes_per_rank": stack_bytes,
                        "hbm_gbs_whole_step": stack_bytes / (ms_step * 1e-3) / 1e9,

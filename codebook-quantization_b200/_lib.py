@@ -45,6 +45,11 @@ SIGNATURES = {
                                               _P, _I64, _INT, _P, ct.c_float, _P, _I64, _P, _P]),
     "cbq_linear_fixed_noalloc": (_INT, [_P, _INT, _I64, _I64, _P, _I64, _P, _I64, _INT, _I64, _I64, _P,
                                         _P, _INT, _I64, _P]),
+    "cbq_host_register": (_INT, [_P, _I64, _INT]),
+    "cbq_host_unregister": (_INT, [_P]),
+    "cbq_streamed_chunk_rows": (_I64, [_I64, _I64, _INT, _I64]),
+    "cbq_linear_fixed_streamed": (_INT, [_P, _INT, _I64, _I64, _P, _I64, _P, _I64, _INT, _I64, _I64, _P, _P,
+                                         _INT, _I64, _P, _I64, _P, _I64, _P]),
     "cbq_embedding_fixed": (_INT, [_P, _I64, _P, _I64, _P, _I64, _INT, _I64, _I64, _P, _INT, _P, _P]),
     "cbq_unpack_fixed": (_INT, [_P, _I64, _INT, _I64, _P, _P]),
     "cbq_pack_fixed": (_INT, [_P, _I64, _INT, _P, _I64, _P]),

@@ -13,12 +13,17 @@ and the embedding's ``embed_scale`` and output dtype (the codebook buffer's).
 
 Changed on purpose: ``direct_codebook`` tensors always run on the GPU through
 ``libcbq``.  There is no CPU or decode-at-load fallback: ``use_gpu=False`` or a
-missing CUDA device raises instead of silently switching path, and ``use_mmap``
-/ ``idx_file`` are accepted and ignored, as the reference ignores them whenever
-its GPU path is active (``:265-267``).
+missing CUDA device raises instead of silently switching path.  ``use_mmap``
+with an existing ``idx_file`` (a flat ``.idx`` of the packed indices) keeps a
+fixed-width stream in host memory -- the mapped file, page-locked -- and
+streams it to the GPU on every forward (``HostStreamedLinear``), where the
+reference runs its CPU kernel on the mapping (``:137-140``, ``:268-274``);
+otherwise the stream is copied to device memory, as the reference's GPU path
+does (``:265-267``).
 """
 from __future__ import annotations
 
+from pathlib import Path
 from typing import Tuple
 
 import numpy as np
@@ -82,6 +87,7 @@ class AdaptiveCodebookLinear(nn.Module):
         self.bits = 8
         self._gpu_func = None
         self._huff_data = None
+        self._mmap_buf = None   # MmappedPackedBuffer of the .idx file when use_mmap=True
 
     @property
     def in_features(self) -> int:
@@ -126,6 +132,10 @@ class AdaptiveCodebookLinear(nn.Module):
                     name, data["huff_stream"], data["huff_lengths"], int(np.asarray(data["huff_n"])[0]),
                     cb, shape, layer.bits, device=device,
                     **{k: data.get(k) for k in _HUFF_TABLE_KEYS})
+            elif use_mmap and idx_file is not None and Path(idx_file).exists():
+                from .host_stream import HostStreamedLinear, MmappedPackedBuffer
+                layer._mmap_buf = MmappedPackedBuffer(idx_file)
+                layer._gpu_func = HostStreamedLinear(name, layer._mmap_buf, cb, shape, layer.bits, device=device)
             else:
                 layer._gpu_func = GPUAcceleratedLinear(name, data["indices"], cb, shape, layer.bits,
                                                        device=device)

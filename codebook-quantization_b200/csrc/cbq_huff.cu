@@ -121,8 +121,12 @@ __global__ void __launch_bounds__(128) k_huff_chunks(const uint8_t *stream, uint
     }
     if (K) quarter[r * nch + nch - 1] = quarters;
     if (bad) report(status, CBQ_FLAG_CORRUPT, (uint32_t)r);
+    // The last row ends inside the stream's final bytes: within 8 bits of the
+    // end for a stream as the encoder writes it, within 16 for a row shard
+    // cut from the tail of one (the source's up to 7 padding bits, plus up to
+    // 7 more from the shard's own byte rounding).
     const bool last = (r + 1 == M);
-    const bool end_ok = last ? (pos <= total_bits && pos > total_bits - 8) || (K == 0)
+    const bool end_ok = last ? (pos <= total_bits && pos > total_bits - 16) || (K == 0)
                              : (pos == rbs[r + 1]);
     if (!end_ok || overflow) report(status, CBQ_FLAG_ROW_END, (uint32_t)r);
 }

@@ -372,6 +372,19 @@ class Qwen3Decoder:
             per = 6 + attn                # the same with two RMSNorm launches (after NCCL at TP > 1)
         return 2 + per * n + 1            # embedding + first RMSNorm, the layers, lm_head
 
+    def layer_launches(self) -> str:
+        """The launches of one decoder layer of the step, in order."""
+        if not self.fused:
+            return "one per linear layer, torch operations around them"
+        attn = "attention (q/k norm + rope, split keys)" if self.fuse_rope else "q/k norm + rope, attention"
+        if self.prenorm:
+            return f"q/k/v (+ input norm), {attn}, o (+ residual), gate/up (+ norm, SiLU*up), down (+ residual)"
+        if self.w.huffman or self.B > 2:
+            return f"q, k, v, {attn}, o, norm, gate, up, down, norm"
+        norm = " + norm" if self.fuse_norm else ", norm"
+        ar = " (peer all-reduce)" if self.peer is not None else (" + NCCL all-reduce" if self.world > 1 else "")
+        return f"q/k/v, {attn}, o{ar}{norm}, gate/up, down{ar}{norm}"
+
     def step(self, ids: torch.Tensor, pos: int) -> torch.Tensor:
         """Eager step (no graph): returns the greedy next ids [B]."""
         self.ids.copy_(ids)

@@ -194,6 +194,39 @@ int cbq_linear_fixed_residual_norm(const void *x_dev, int x_dtype, int64_t T, in
                                    float eps, void *norm_out_dev, int64_t ldn, uint32_t *arrive_dev,
                                    void *stream);
 
+/* ---- host-resident streams (models whose packed indices exceed device memory) ----
+ * The reference memory-maps flat .idx files (raw `indices` bytes) and runs its
+ * CPU kernel on the mapping (src/compressed_matmul_cpu.py:23-63,
+ * src/adaptive_compressor.py:1254-1316).  Here the stream stays in host
+ * memory and is copied to the device in row chunks per call. */
+
+/* Page-locks [host_ptr, host_ptr + bytes) for asynchronous copies
+ * (cudaHostRegister; read_only != 0 for a read-only mapping such as a
+ * memory-mapped .idx file, CBQ_ERR_UNSUPPORTED where the device cannot).
+ * cbq_host_unregister undoes it. */
+int cbq_host_register(void *host_ptr, int64_t bytes, int read_only);
+int cbq_host_unregister(void *host_ptr);
+
+/* Rows per chunk of cbq_linear_fixed_streamed for a staging buffer of
+ * staging_bytes (two halves), or -1 (K % 128 != 0, or not one row fits). */
+int64_t cbq_streamed_chunk_rows(int64_t M, int64_t K, int bits, int64_t staging_bytes);
+
+/* cbq_linear_fixed with the packed stream in HOST memory (packed_host:
+ * ceil(M*K*bits/8) bytes, pinned or registered for the copies to overlap).
+ * Row chunks are copied into the two halves of staging_dev (device, 256-byte
+ * aligned) on a copy stream of the library, each chunk's copy overlapping the
+ * previous chunk's GEMV on `stream`; the GEMV of a chunk is cbq_linear_fixed
+ * over its rows (workspace_dev as there, sized for one chunk's rows; may be
+ * NULL).  Copies start after the work already queued on `stream`; calls on
+ * one device are serialised by a lock.  K % 128 == 0, else
+ * CBQ_ERR_UNSUPPORTED.  No counterpart on the reference's GPU path (its mmap
+ * path runs on the CPU). */
+int cbq_linear_fixed_streamed(const void *x_dev, int x_dtype, int64_t T, int64_t ldx, const uint8_t *packed_host,
+                              int64_t packed_bytes, const float *codebook_dev, int64_t C, int bits, int64_t M,
+                              int64_t K, const float *bias_dev, void *out_dev, int out_dtype, int64_t ldo,
+                              void *staging_dev, int64_t staging_bytes, void *workspace_dev,
+                              int64_t workspace_bytes, void *stream);
+
 /* Size of the device array built into the library that
  * cbq_linear_fixed_noalloc uses as its workspace (8 MiB on every GPU that
  * loads the library, until the process exits). */
@@ -279,8 +312,9 @@ int64_t cbq_huff_chunk_table_words(int64_t M, int64_t K);
  * The reference format has only per-row entry points
  * (src/huffman_codebook.py:213); this table gives the GEMV its 64- and
  * 16-symbol entry points.  Records CBQ_FLAG_ROW_END when a row does not end
- * where the next one starts and CBQ_FLAG_CORRUPT for undecodable codes, in
- * status_dev. */
+ * where the next one starts (the last row: when it does not end within the
+ * final 16 bits of total_bits, which admits row shards cut from the tail of a
+ * stream) and CBQ_FLAG_CORRUPT for undecodable codes, in status_dev. */
 int cbq_huff_chunk_table(const uint8_t *stream_dev, int64_t stream_bytes,
                          const void *tables_dev, const int64_t *row_bit_starts_dev,
                          int64_t M, int64_t K, int64_t total_bits,

@@ -76,3 +76,26 @@ def test_model_dir_config_and_layout(tmp_path):
     assert md.read_qwen3_config(tmp_path) == cfg
     assert md.cache_dir_for(tmp_path, False).name == "codebook-lossless"
     assert md.cache_dir_for(tmp_path, True).name == "codebook-lossless-huffman"
+
+
+def test_mmapped_packed_buffer_and_idx_export(tmp_path):
+    """Flat .idx files (the reference's export_flat_idx / MmappedPackedBuffer
+    contract, tests/test_mmap_inference.py): the exported bytes are the
+    .npz's `indices`, the mapping reads them back as a zero-copy view."""
+    hs = cbq.host_stream
+    rng = np.random.default_rng(7)
+    M, K, bits = 64, 32, 13
+    packed = cbq.bitpack.pack_any_bits(rng.integers(0, 1 << bits, size=M * K).astype(np.uint16), bits)
+    tdir = tmp_path / "codebook-lossless" / "tensors"
+    NPZ.save_cached_tensor(tdir / "model_layers_0_mlp_weight.npz", "model.layers.0.mlp.weight",
+                           {"mode": "direct_codebook", "shape": np.array([M, K]), "bits": bits,
+                            "codebook_type": "mlp_ffn", "indices": packed})
+    assert hs.export_flat_idx(tmp_path) == 1
+    assert hs.export_flat_idx(tmp_path) == 0                    # already exported
+    buf = hs.MmappedPackedBuffer(tdir / "model_layers_0_mlp_weight.idx")
+    arr = buf.as_numpy()
+    assert arr.base is not None and len(buf) == packed.size
+    np.testing.assert_array_equal(arr, packed)
+    np.testing.assert_array_equal(arr[100:200], packed[100:200])
+    del arr
+    buf.close()
