@@ -193,6 +193,9 @@ __device__ __forceinline__ void finish_piece(const FixedArgs &a, const float (&t
             if (a.out_bf16) store_out<__nv_bfloat16>(a.out, o, sum + b);
             else store_out<float>(a.out, o, sum + b);
         }
+        // leave the row's pieces and its counter zero, so the workspace stays
+        // zero-filled for the next call whatever its shape
+        for (int i = 0; i < nseg * TB; ++i) pr[i] = 0.f;
         atomicExch(&a.cnt[r], 0u);
     }
 }

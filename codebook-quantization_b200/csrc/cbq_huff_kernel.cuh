@@ -302,6 +302,9 @@ __device__ __forceinline__ void huff_finish_piece(const HuffArgs &a, const float
             for (int s2 = 0; s2 < nseg; ++s2) sum += __ldcg(pr + s2 * TB + t);
             store((a.t0 + t) * a.ldo + r, sum + b);
         }
+        // leave the row's pieces and its counter zero, so the workspace stays
+        // zero-filled for the next call whatever its shape
+        for (int i = 0; i < nseg * TB; ++i) pr[i] = 0.f;
         atomicExch(&a.cnt[r], 0u);
     }
 }

@@ -96,8 +96,9 @@ int64_t cbq_linear_fixed_workspace_bytes(int64_t M, int64_t K, int64_t T);
  *   workspace_dev  NULL, or a zero-filled buffer of at least
  *              cbq_linear_fixed_workspace_bytes(M, K, T) bytes: lets the
  *              kernel balance work at 1024-index granularity instead of
- *              whole rows.  Calls sharing one workspace must not overlap on
- *              the GPU (the same stream is fine). */
+ *              whole rows.  Every call leaves it zero-filled, so calls of
+ *              any shape may share it; calls sharing one workspace must not
+ *              overlap on the GPU (the same stream is fine). */
 int cbq_linear_fixed(const void *x_dev, int x_dtype, int64_t T, int64_t ldx,
                      const uint8_t *packed_dev, int64_t packed_bytes,
                      const float *codebook_dev, int64_t C, int bits,

@@ -173,3 +173,26 @@ def test_gpu_lossless_compressor_roundtrip():
     cb = d["codebook"].cpu().numpy()
     idx = cbq.bitpack.unpack_any_bits(d["indices"].cpu().numpy(), d["bits"], 256 * 512)
     np.testing.assert_array_equal(cb[idx].view(np.uint32) >> 16, bits.cpu().numpy().reshape(-1))
+
+
+def test_workspace_shared_by_calls_of_different_shapes():
+    """One workspace passed to 3..63-token calls of several row counts in turn:
+    every call leaves it zero-filled, so a later call whose counters fall where
+    an earlier call kept its piece sums still combines its rows correctly."""
+    dev = need_cuda()
+    L = cbq._lib
+    K, T, bits = 2048, 8, 13
+    n = L.query("cbq_linear_fixed_workspace_bytes", 1000, K, T)
+    ws = torch.zeros(n, dtype=torch.uint8, device=dev)
+    for M in (1000, 777, 1000, 301, 999):
+        idx, cb, packed = make_case(M, K, bits, seed=M)
+        lin = cbq.GPUAcceleratedLinear("w", packed, cb, (M, K), bits, device=dev)
+        x = np.random.default_rng(M).standard_normal((T, K)).astype(np.float32)
+        xd = torch.from_numpy(x).to(dev)
+        out = torch.empty(T, M, device=dev)
+        L.call("cbq_linear_fixed", xd.data_ptr(), L.CBQ_F32, T, K, lin.packed.data_ptr(), lin.nbytes,
+               lin.codebook.data_ptr(), lin.C, bits, M, K, None, out.data_ptr(), L.CBQ_F32, M, ws.data_ptr(), n,
+               torch.cuda.current_stream(dev).cuda_stream)
+        torch.cuda.synchronize()
+        assert rel_l2(out.cpu().numpy(), oracle.linear_fixed(x, packed, cb, M, K, bits)) < 1e-5, M
+    assert not bool(ws.any())

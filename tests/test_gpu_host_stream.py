@@ -32,7 +32,7 @@ def _case(M, K, bits, seed):
 @pytest.mark.parametrize("M,K,bits,T,dt,staging", [(3000, 1024, 13, 1, torch.bfloat16, 1 << 20),
                                                    (1000, 4096, 12, 2, torch.float32, 3 << 20),
                                                    (777, 2048, 13, 8, torch.bfloat16, 1 << 20),
-                                                   (500, 512, 8, 64, torch.bfloat16, 1 << 18)])
+                                                   (900, 512, 8, 64, torch.bfloat16, 1 << 18)])
 def test_host_streamed_matches_device_resident(tmp_path, src, M, K, bits, T, dt, staging):
     dev = need_cuda()
     packed, cb = _case(M, K, bits, seed=M + K + T)
