@@ -416,22 +416,53 @@ __global__ void __launch_bounds__(D) k_attn_decode(const T *q, T *k_cache, T *v_
     __syncthreads();
     if (!last) return;
     __threadfence();
+    // combine: every chunk's (m, l) into shared memory with independent loads,
+    // then per head M = max m_s, L = sum_s l_s exp(m_s - M) and the weight
+    // f_s = exp(m_s - M) / L of each chunk (chunk order), then thread i adds
+    // its dimension of the S chunks' acc with all loads issued first
     const float *pb = sp.part + (int64_t)bg * S * PW;
+    float *fw = sc;                                   // [S][G] chunk weights (the scores are consumed)
+    for (int e = threadIdx.x; e < S * G; e += D) {
+        const int t = e / G, h = e - (e / G) * G;
+        fw[e] = __ldcg(pb + (int64_t)t * PW + G * D + h);
+        fw[S * G + e] = __ldcg(pb + (int64_t)t * PW + G * D + G + h);
+    }
+    __syncthreads();
+    if (threadIdx.x < G) {
+        const int h = threadIdx.x;
+        float M = -INFINITY;
+        for (int t = 0; t < S; ++t) M = fmaxf(M, fw[t * G + h]);
+        float lsum = 0.f;
+        for (int t = 0; t < S; ++t) {
+            const float mt = fw[t * G + h];
+            const float f = mt == -INFINITY ? 0.f : expf(mt - M);
+            fw[2 * S * G + t * G + h] = f;
+            lsum = fmaf(fw[S * G + t * G + h], f, lsum);
+        }
+        stat[h][1] = lsum;
+    }
+    __syncthreads();
+    float o[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) o[h] = 0.f;
+    constexpr int CB = 8;                             // chunks whose loads are issued together
+    for (int t0 = 0; t0 < S; t0 += CB) {
+        float av[CB][G];
+#pragma unroll
+        for (int u = 0; u < CB; ++u)
+#pragma unroll
+            for (int h = 0; h < G; ++h)
+                av[u][h] = t0 + u < S ? __ldcg(pb + (int64_t)(t0 + u) * PW + h * D + i) : 0.f;
+#pragma unroll
+        for (int u = 0; u < CB; ++u)
+#pragma unroll
+            for (int h = 0; h < G; ++h)
+                if (t0 + u < S) o[h] = fmaf(av[u][h], fw[2 * S * G + (t0 + u) * G + h], o[h]);
+    }
 #pragma unroll
     for (int h = 0; h < G; ++h) {
-        float M = -INFINITY;
-        for (int t = 0; t < S; ++t) M = fmaxf(M, __ldcg(pb + (int64_t)t * PW + G * D + h));
-        float lsum = 0.f, o = 0.f;
-        if (M > -INFINITY) {
-            for (int t = 0; t < S; ++t) {
-                const float mt = __ldcg(pb + (int64_t)t * PW + G * D + h);
-                if (mt == -INFINITY) continue;
-                const float f = expf(mt - M);
-                lsum = fmaf(__ldcg(pb + (int64_t)t * PW + G * D + G + h), f, lsum);
-                o = fmaf(__ldcg(pb + (int64_t)t * PW + h * D + i), f, o);
-            }
-        }
-        ob[h * D + i] = from_f32<T>(lsum > 0.f ? o / lsum : 0.f);
+        const float lsum = stat[h][1];
+        ob[h * D + i] = from_f32<T>(lsum > 0.f ? o[h] / lsum : 0.f);
     }
     if (threadIdx.x == 0) sp.count[bg] = 0u;          // ready for the next launch
 }
@@ -557,7 +588,8 @@ int launch_attn(const void *q_dev, void *k_cache_dev, void *v_cache_dev, int dty
         sp.count = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(ws) +
                                                 cbq_host::align_up(B * Hkv * S * (G * head_dim + 2 * G) * 4, 256));
     }
-    const size_t smem = (size_t)sp.cmax * 4 * (size_t)G;       // scores of the group's heads
+    // scores of the group's heads; the combining CTA reuses it for 3 * S * G chunk values
+    const size_t smem = std::max((size_t)sp.cmax * 4 * (size_t)G, (size_t)(S > 1 ? 3 * S * G * 4 : 0));
     if (smem > (size_t)cbq_host::max_smem_optin() - 4096 - (ROPE ? (size_t)G * head_dim * 4 : 0))
         return CBQ_ERR_UNSUPPORTED;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
