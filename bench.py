@@ -125,10 +125,10 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
-            time.sleep(0.1)
+            time.sleep(0.3)                     # the sampler is running before the timed work starts
         except OSError:
             self.proc = None
         return self
@@ -599,10 +599,10 @@ def tp_token_check(cbq, dev, rank, world, group):
         ok, why = True, ""
         try:
             full = q3.CompressedQwen3Weights(cfg, dev, huffman=huffman, seed=3)
-            ref = qd.Qwen3Decoder(full, batch=2, max_len=40, act_dtype=torch.float32).generate(prompt, 30).cpu()
+            ref = qd.Qwen3Decoder(full, batch=2, max_len=48, act_dtype=torch.float32).generate(prompt, 30).cpu()
             del full
             Wt = q3.CompressedQwen3Weights(cfg, dev, huffman=huffman, rank=rank, world=world, seed=3)
-            dec = qd.Qwen3Decoder(Wt, batch=2, max_len=40, act_dtype=torch.float32, group=group, allreduce=allreduce)
+            dec = qd.Qwen3Decoder(Wt, batch=2, max_len=48, act_dtype=torch.float32, group=group, allreduce=allreduce)
             if allreduce == "peer" and dec.peer is None:
                 ok, why = False, "peer path not taken"
             eager = dec.generate(prompt, 30).cpu()

@@ -326,7 +326,7 @@ int linear_fixed_multi_impl(const void *x_dev, int x_dtype, int64_t T, int64_t l
                             const float *codebook_dev, int64_t C, int bits, int64_t K,
                             const float *const *bias_dev, void *const *out_dev, const int64_t *ldo,
                             const void *const *resid_dev, int out_dtype, int epilogue, int pn_on,
-                            const float *pn_w, float pn_eps, void *stream) {
+                            const float *pn_w, float pn_eps, void *stream, const GemvArgs *ar = nullptr) {
     if (nmat < 1 || nmat > kGvMaxMats || !packed_dev || !packed_bytes || !M || !out_dev || !ldo)
         return CBQ_ERR_ARG;
     if (T < 0 || K < 0 || bits < 1 || bits > 16 || C < 1 || C > 65536) return CBQ_ERR_ARG;
@@ -360,6 +360,11 @@ int linear_fixed_multi_impl(const void *x_dev, int x_dtype, int64_t T, int64_t l
     a.out_bf16 = out_dtype == CBQ_BF16;
     a.H = g.H; a.NP = g.NP; a.m128 = 128u; a.m4 = 4u; a.status = nullptr;
     a.pn_on = pn_on; a.pn_w = pn_w; a.pn_eps = pn_eps;
+    if (ar) {
+        a.ar_on = 1; a.ar_world = ar->ar_world; a.ar_slots = ar->ar_slots; a.ar_counts = ar->ar_counts;
+        a.ar_epoch = ar->ar_epoch; a.ar_expect = ar->ar_expect; a.ar_resid = ar->ar_resid;
+        a.status = ar->status;
+    }
     return launch_gemv(bits, (int)T, g.nf, x_dtype == CBQ_BF16, a, g.smem, g.grid,
                        static_cast<cudaStream_t>(stream));
 }
@@ -386,6 +391,24 @@ extern "C" int cbq_linear_fixed_multi_norm(const void *x_dev, int x_dtype, int64
     return linear_fixed_multi_impl(x_dev, x_dtype, T, ldx, nmat, packed_dev, packed_bytes, M, codebook_dev, C,
                                    bits, K, bias_dev, out_dev, ldo, resid_dev, out_dtype, epilogue, 1,
                                    norm_weight_dev, eps, stream);
+}
+
+extern "C" int cbq_linear_fixed_multi_allreduce_norm(
+    const void *x_dev, int x_dtype, int64_t T, int64_t ldx, int nmat, const uint8_t *const *packed_dev,
+    const int64_t *packed_bytes, const int64_t *M, const float *codebook_dev, int64_t C, int bits, int64_t K,
+    const float *const *bias_dev, void *const *out_dev, const int64_t *ldo, const void *const *resid_dev,
+    int out_dtype, int epilogue, const float *norm_weight_dev, float eps, int world, const void *resid_in_dev,
+    const void *local_slots_dev, const uint32_t *local_counts_dev, const uint32_t *epoch_dev, int64_t expect,
+    uint32_t *status_dev, void *stream) {
+    if (world < 1 || world > kGvMaxPeers || !resid_in_dev || !local_slots_dev || !local_counts_dev || !epoch_dev ||
+        expect < 1 || expect > 0xffffffffll || resid_in_dev == x_dev)
+        return CBQ_ERR_ARG;
+    GemvArgs ar{};
+    ar.ar_world = world; ar.ar_slots = local_slots_dev; ar.ar_counts = local_counts_dev; ar.ar_epoch = epoch_dev;
+    ar.ar_expect = (uint32_t)expect; ar.ar_resid = resid_in_dev; ar.status = status_dev;
+    return linear_fixed_multi_impl(x_dev, x_dtype, T, ldx, nmat, packed_dev, packed_bytes, M, codebook_dev, C,
+                                   bits, K, bias_dev, out_dev, ldo, resid_dev, out_dtype, epilogue, 1,
+                                   norm_weight_dev, eps, stream, &ar);
 }
 
 namespace {

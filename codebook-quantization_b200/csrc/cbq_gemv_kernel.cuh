@@ -134,6 +134,19 @@ struct GemvArgs {
     int pn_on;
     const float *pn_w;   // [K] or null (unit weights)
     float pn_eps;
+    // Tensor-parallel all-reduce consumed on load (with pn_on): before the
+    // norm, every CTA waits (bounded) until ar_counts[s] >= *ar_epoch *
+    // ar_expect for every rank s, then forms x[t] = round(ar_resid[t] +
+    // round(sum_s slot_s[t])) in rank order (slot s row t at ar_slots + (s *
+    // ntok + t) * K) and writes it to a.x (every CTA the same values; a.x is
+    // not ar_resid), from where the launch loads it.
+    int ar_on;
+    int ar_world;
+    const void *ar_slots;
+    const uint32_t *ar_counts;
+    const uint32_t *ar_epoch;
+    uint32_t ar_expect;
+    const void *ar_resid;
 };
 
 // The norm of GemvNorm, run by the last CTA (all its threads).  red: 16
@@ -370,6 +383,52 @@ __device__ __forceinline__ void gv_load_x(const __nv_bfloat16 *xr, int k0, int K
 // The activation pre-norm of GemvArgs: scale[t] = rsqrt(mean(x[t]^2) + eps)
 // for the launch's tokens, every CTA the same value (thread i adds elements
 // i, i + blockDim, ... in order, then a fixed tree).  All threads call it.
+// The all-reduce of GemvArgs (ar_*), run by every CTA before the norm:
+// returns false (and records CBQ_FLAG_TIMEOUT) when a rank's rows did not
+// arrive within the bound, or an earlier wait of this run already gave up.
+template <typename XT, int TB>
+__device__ __forceinline__ bool gv_allreduce_in(const GemvArgs &a, int *late) {
+    const int tid = threadIdx.x;
+    if (tid == 0)
+        *late = (a.status && (*(volatile uint32_t *)(a.status + CBQ_STATUS_FLAGS) & CBQ_FLAG_TIMEOUT)) ? 1 : 0;
+    __syncthreads();
+    if (!*late && tid < a.ar_world) {
+        const uint32_t want = *a.ar_epoch * a.ar_expect;
+        const uint64_t t0 = global_timer_ns();
+        while (true) {
+            uint32_t c;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(c) : "l"(a.ar_counts + tid) : "memory");
+            if ((int32_t)(c - want) >= 0) break;
+            if (global_timer_ns() - t0 > kWaitNs) {
+                *late = 1;
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    __syncthreads();
+    if (*late) {
+        if (tid == 0 && blockIdx.x == 0) report(a.status, CBQ_FLAG_TIMEOUT, 0u);
+        return false;
+    }
+    __threadfence_system();
+    const XT *slots = static_cast<const XT *>(a.ar_slots);
+    const XT *res = static_cast<const XT *>(a.ar_resid);
+    XT *xo = const_cast<XT *>(static_cast<const XT *>(a.x));
+    for (int t = 0; t < a.ntok; ++t) {
+        for (int k = tid; k < a.K; k += kGvWarps * 32) {
+            float sum = 0.f;
+            for (int p = 0; p < a.ar_world; ++p)
+                sum += to_f32<XT>(__ldcg(slots + ((int64_t)p * a.ntok + t) * a.K + k));
+            const float v = to_f32<XT>(from_f32<XT>(to_f32<XT>(res[(a.t0 + t) * a.ldx + k]) +
+                                                     to_f32<XT>(from_f32<XT>(sum))));
+            xo[(a.t0 + t) * a.ldx + k] = from_f32<XT>(v);
+        }
+    }
+    __syncthreads();                                       // this CTA's x rows, before it reads them
+    return true;
+}
+
 template <typename XT, int TB>
 __device__ __forceinline__ void gv_prenorm_scales(const GemvArgs &a, float (&scale)[TB], float *red) {
     const XT *x = static_cast<const XT *>(a.x);
@@ -505,7 +564,12 @@ __global__ void __launch_bounds__(kGvWarps * 32, 1) k_gemv_fixed(const GemvArgs 
     float pn_scale[TB];
 #pragma unroll
     for (int t = 0; t < TB; ++t) pn_scale[t] = 1.f;
-    if (a.pn_on) {
+    bool ar_ok = true;
+    if (a.ar_on) {
+        __shared__ int ar_late;
+        ar_ok = gv_allreduce_in<XT, TB>(a, &ar_late);
+    }
+    if (a.pn_on && ar_ok) {
         __shared__ float pn_red[kGvWarps];
         gv_prenorm_scales<XT, TB>(a, pn_scale, pn_red);
     }

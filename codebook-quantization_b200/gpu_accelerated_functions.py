@@ -157,7 +157,8 @@ class GPUAcceleratedLinear:
         return res if res.dtype == want else res.to(want)
 
 
-def linear_fixed_multi(mats, x: torch.Tensor, outs, epilogue: int = 0, resids=None, norm=None) -> bool:
+def linear_fixed_multi(mats, x: torch.Tensor, outs, epilogue: int = 0, resids=None, norm=None,
+                       allreduce=None) -> bool:
     """One launch of ``cbq_linear_fixed_multi`` over ``mats`` (GPUAcceleratedLinear
     objects sharing K, bits and codebook) for ``x [T, K]``.  ``outs[i]`` are
     ``[T, M_i]`` tensors (for ``CBQ_EPI_SILU_MUL`` only ``outs[0]`` is
@@ -166,7 +167,11 @@ def linear_fixed_multi(mats, x: torch.Tensor, outs, epilogue: int = 0, resids=No
     un-normalised residual stream and the launch applies the RMSNorm as it
     loads it (``cbq_linear_fixed_multi_norm``).  Returns False, having
     launched nothing, when the shape is outside what the fused kernel supports
-    (T > 2, unaligned rows); the caller then runs the matrices one by one."""
+    (T > 2, unaligned rows); the caller then runs the matrices one by one.
+    ``allreduce=(world, resid_in, slots_ptr, counts_ptr, epoch_ptr, expect,
+    status_ptr)`` (with ``norm``): ``x`` receives round(resid_in + the
+    all-reduced partial rows) before the normalised GEMV reads it
+    (``cbq_linear_fixed_multi_allreduce_norm``)."""
     import ctypes as ct
     n = len(mats)
     m0 = mats[0]
@@ -191,7 +196,14 @@ def linear_fixed_multi(mats, x: torch.Tensor, outs, epilogue: int = 0, resids=No
     rp = None if resids is None else (P * n)(*[r.data_ptr() for r in resids])
     common = (x2.data_ptr(), xcode, T, x2.stride(0) if T > 1 else m0.K, n, packed, nbytes, Ms,
               m0.codebook.data_ptr(), m0.C, m0.bits, m0.K, None, optrs, ldo, rp, ocode, int(epilogue))
-    if norm is None:
+    if allreduce is not None:
+        fn = "cbq_linear_fixed_multi_allreduce_norm"
+        w, eps = norm
+        world, resid_in, slots, counts, epoch, expect, status = allreduce
+        rc = _lib.lib().cbq_linear_fixed_multi_allreduce_norm(
+            *common, None if w is None else w.data_ptr(), float(eps), int(world), resid_in.data_ptr(), slots,
+            counts, epoch, int(expect), status, device_stream(m0.device))
+    elif norm is None:
         fn = "cbq_linear_fixed_multi"
         rc = _lib.lib().cbq_linear_fixed_multi(*common, device_stream(m0.device))
     else:

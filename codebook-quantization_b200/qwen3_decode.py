@@ -85,6 +85,17 @@ class _PeerAllReduce:
         torch.cuda.synchronize(dec.dev)
         dist.barrier(group=dec.group)
 
+    def produce(self, site: int, lin, x):
+        """The row-parallel GEMV whose epilogue stores its partial rows into
+        slot ``rank`` of every rank's buffer for ``site`` and counts them."""
+        dec = self.dec
+        rc = _lib.lib().cbq_linear_fixed_peer(
+            x.data_ptr(), dec.code, dec.B, x.shape[1], lin.packed.data_ptr(), lin.nbytes, lin.codebook.data_ptr(),
+            lin.C, lin.bits, lin.M, lin.K, None, self.W, self.slots[site], self.counts[site], lin.M, dec.code,
+            device_stream(dec.dev))
+        if rc != _lib.CBQ_OK:
+            raise _lib.CbqError("cbq_linear_fixed_peer", rc)
+
     def run(self, site: int, lin, x):
         dec = self.dec
         W = self.W
@@ -186,6 +197,12 @@ class Qwen3Decoder:
         self.peer = None
         if fused and self.world > 1 and allreduce == "peer" and not weights.huffman and batch <= 2:
             self.peer = _PeerAllReduce(self, 2 * cfg.layers)
+        # tensor parallel over peer memory: each all-reduce is consumed inside
+        # the next GEMV launch (cbq_linear_fixed_multi_allreduce_norm), which
+        # writes the updated residual stream into the other of two buffers
+        self.peer_prenorm = self.peer is not None and prenorm and not fuse_norm
+        if self.peer_prenorm:
+            self.xr = (self.x, torch.zeros_like(self.x))
         L = weights.layers
         self.emb = L["model.embed_tokens.weight"]
         self.lm_head = L["lm_head.weight"]
@@ -282,6 +299,8 @@ class Qwen3Decoder:
         self.emb(self.ids, out=self.x)
         if self.prenorm:
             return self._step_prenorm()
+        if self.peer_prenorm:
+            return self._step_peer_prenorm()
         self._rmsnorm(self.x, self.h)
         for li, (q_p, k_p, v_p, o_p, g_p, u_p, d_p) in enumerate(self.layer_mods):
             self._linear((q_p, k_p, v_p), (self.q, self.k, self.v))
@@ -343,6 +362,49 @@ class Qwen3Decoder:
             self._rmsnorm(self.x, self.h)
             self._finish(self.lm_head(self.h))
 
+    def _consume(self, site: int, j: int, mats, outs, epilogue=_lib.CBQ_EPI_STORE) -> int:
+        """The GEMV that consumes all-reduce ``site``: reads residual buffer
+        j % 2 plus every rank's partial rows, writes buffer (j + 1) % 2,
+        normalises and multiplies; returns the next consumer index."""
+        pr = self.peer
+        W = pr.W
+        src, dst = self.xr[j % 2], self.xr[(j + 1) % 2]
+        ar = (W, src, pr.local + site * W * pr.slot_bytes, pr.local + pr.data + site * W * 4,
+              pr.epoch.data_ptr(), self.cfg.hidden, pr.status.data_ptr())
+        if not linear_fixed_multi(mats, dst, outs, epilogue, norm=(None, self.cfg.rms_eps), allreduce=ar):
+            raise RuntimeError("tensor-parallel all-reduce GEMV: shape not supported by the fused kernel")
+        return j + 1
+
+    def _step_peer_prenorm(self):
+        """Tensor parallel over peer memory, five launches per layer: q/k/v
+        (consuming the previous layer's down_proj all-reduce, norm inside),
+        attention, o_proj writing its partial rows to every rank, gate/up
+        (consuming o_proj's all-reduce, norm inside), down_proj writing its
+        partial rows to every rank; lm_head consumes the last all-reduce."""
+        cfg, B, d = self.cfg, self.B, self.cfg.head_dim
+        stream = device_stream(self.dev)
+        ws, nws = self.attn_ws.data_ptr(), self.attn_ws.numel()
+        j = 0
+        for li, (q_p, k_p, v_p, o_p, g_p, u_p, d_p) in enumerate(self.layer_mods):
+            if li == 0:
+                if not linear_fixed_multi((q_p, k_p, v_p), self.xr[0], (self.q, self.k, self.v),
+                                          norm=(None, cfg.rms_eps)):
+                    raise RuntimeError("q/k/v GEMV: shape not supported by the fused kernel")
+            else:
+                j = self._consume(2 * li - 1, j, (q_p, k_p, v_p), (self.q, self.k, self.v))
+            _lib.call("cbq_attn_decode_rope_split", self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(),
+                      self.code, B, self.hl, self.kvl, d, float(cfg.rms_eps), None, None, self.cos.data_ptr(),
+                      self.sin.data_ptr(), self.pos.data_ptr(), self.k_cache[li].data_ptr(),
+                      self.v_cache[li].data_ptr(), self.max_len, float(d ** -0.5), self.a.data_ptr(), ws, nws,
+                      stream)
+            self.peer.produce(2 * li, o_p, self.a)
+            j = self._consume(2 * li, j, (g_p, u_p), (self.m,), _lib.CBQ_EPI_SILU_MUL)
+            self.peer.produce(2 * li + 1, d_p, self.m)
+        if not isinstance(self.lm_head, GPUAcceleratedLinear):
+            raise RuntimeError("lm_head must be fixed width on the peer-memory path")
+        self._consume(2 * cfg.layers - 1, j, (self.lm_head,), (self.logits_buf,))
+        self._finish(self.logits_buf)
+
     def _finish(self, logits):
         self.logits = logits
         val, idx = logits.float().max(dim=-1)
@@ -362,7 +424,7 @@ class Qwen3Decoder:
         if not self.fused:
             return 1 + 7 * n + 1          # embedding, 7 linears per layer, lm_head
         attn = 1 if self.fuse_rope else 2
-        if self.prenorm:                  # embedding, 5 per layer (norms inside the GEMVs), lm_head
+        if self.prenorm or self.peer_prenorm:   # embedding, 5 per layer (norms inside the GEMVs), lm_head
             return 1 + 5 * n + 1
         if self.w.huffman or self.B > 2:  # one launch per linear, separate RMSNorms
             per = 3 + attn + 1 + 2 + 1 + 2
@@ -379,6 +441,9 @@ class Qwen3Decoder:
         attn = "attention (q/k norm + rope, split keys)" if self.fuse_rope else "q/k norm + rope, attention"
         if self.prenorm:
             return f"q/k/v (+ input norm), {attn}, o (+ residual), gate/up (+ norm, SiLU*up), down (+ residual)"
+        if self.peer_prenorm:
+            return (f"q/k/v (+ all-reduce of down, norm), {attn}, o (partial rows to every rank), "
+                    f"gate/up (+ all-reduce of o, norm, SiLU*up), down (partial rows to every rank)")
         if self.w.huffman or self.B > 2:
             return f"q, k, v, {attn}, o, norm, gate, up, down, norm"
         norm = " + norm" if self.fuse_norm else ", norm"

@@ -146,6 +146,25 @@ int cbq_linear_fixed_multi_norm(const void *x_dev, int x_dtype, int64_t T, int64
                                 const void *const *resid_dev, int out_dtype, int epilogue,
                                 const float *norm_weight_dev, float eps, void *stream);
 
+/* cbq_linear_fixed_multi_norm whose input is the tensor-parallel all-reduce
+ * of the row-parallel layer before it (the consumer of
+ * cbq_linear_fixed_peer): every CTA waits, bounded (2 s; CBQ_FLAG_TIMEOUT in
+ * status_dev, after which later calls do not wait), until
+ * local_counts_dev[s] >= *epoch_dev * expect for every rank s < world, then
+ * forms x[t] = round(resid_in[t] + round(sum_s slot_s[t])) in rank order
+ * (slot s row t at local_slots_dev + (s * T + t) * K elements), writes it to
+ * x_dev (the updated residual stream; resid_in_dev is a different buffer,
+ * same ldx) and runs the normalised GEMV on it.  One launch replaces the
+ * all-reduce consumer, the RMSNorm and the GEMV.  No counterpart in the
+ * reference (single device). */
+int cbq_linear_fixed_multi_allreduce_norm(
+    const void *x_dev, int x_dtype, int64_t T, int64_t ldx, int nmat, const uint8_t *const *packed_dev,
+    const int64_t *packed_bytes, const int64_t *M, const float *codebook_dev, int64_t C, int bits, int64_t K,
+    const float *const *bias_dev, void *const *out_dev, const int64_t *ldo, const void *const *resid_dev,
+    int out_dtype, int epilogue, const float *norm_weight_dev, float eps, int world, const void *resid_in_dev,
+    const void *local_slots_dev, const uint32_t *local_counts_dev, const uint32_t *epoch_dev, int64_t expect,
+    uint32_t *status_dev, void *stream);
+
 /* Tensor-parallel row-parallel layer (o_proj, down_proj), fused with the
  * data movement of its all-reduce: the GEMV of this rank's K-block writes its
  * partial product [T, M] into every rank's slot for this rank

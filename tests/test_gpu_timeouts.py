@@ -1,8 +1,9 @@
 """The bounded device-side waits of the tensor-parallel all-reduce run out
 cleanly on one GPU.
 
-The consumer of the peer-memory all-reduce (``cbq_rmsnorm_allreduce``, and
-the last CTA of ``cbq_linear_fixed_peer_norm``) polls per-rank arrival
+The consumers of the peer-memory all-reduce (``cbq_rmsnorm_allreduce``, the
+last CTA of ``cbq_linear_fixed_peer_norm``, and every CTA of
+``cbq_linear_fixed_multi_allreduce_norm``) poll per-rank arrival
 counters until they reach ``epoch * expect``.  Here no rank ever adds to the
 counters, so the wait must give up after its bound (2 s of %globaltimer),
 record ``CBQ_FLAG_TIMEOUT`` in the status word, write nothing, and leave the
@@ -107,5 +108,35 @@ def test_peer_norm_gemv_wait_runs_out():
     assert torch.equal(resid, resid0)                 # the residual stream is untouched
     assert int(arrive.item()) == 0                    # the arrival count is left reset
     assert counts.cpu().tolist() == [M, M]            # its own rows were delivered
+    dt2 = _timed(call)
+    assert dt2 < 1.0, dt2
+
+
+def test_allreduce_consuming_gemv_wait_runs_out():
+    """cbq_linear_fixed_multi_allreduce_norm (the GEMV that consumes the
+    previous layer's peer all-reduce): its CTAs' wait gives up, the updated
+    residual stream is not written, and a later call does not wait."""
+    dev = need_cuda()
+    world, T, M, K, bits = 2, 1, 384, 512, 13
+    rng = np.random.default_rng(5)
+    idx = rng.integers(0, 1 << bits, size=M * K).astype(np.uint16)
+    cb = torch.from_numpy(rng.standard_normal(1 << bits).astype(np.float32)).to(dev)
+    lin = cbq.GPUAcceleratedLinear("w", cbq.bitpack.pack_any_bits(idx, bits), cb, (M, K), bits, device=dev)
+    resid_in = torch.randn(T, K, device=dev).to(torch.bfloat16)
+    x = torch.full((T, K), 3.0, device=dev).to(torch.bfloat16)
+    slots = torch.randn(world * T * K, device=dev).to(torch.bfloat16)
+    counts = torch.zeros(world, dtype=torch.int32, device=dev)       # no rank ever arrives
+    epoch = torch.ones(1, dtype=torch.int32, device=dev)
+    out = torch.empty(T, M, device=dev, dtype=torch.bfloat16)
+    status = _status(dev)
+    ar = (world, resid_in, slots.data_ptr(), counts.data_ptr(), epoch.data_ptr(), K, status.data_ptr())
+
+    def call():
+        assert cbq.gpu_accelerated_functions.linear_fixed_multi([lin], x, [out], norm=(None, 1e-6), allreduce=ar)
+    dt1 = _timed(call)
+    st = status.cpu().numpy()
+    assert st[0] & L.FLAG_TIMEOUT, st
+    assert 1.5 < dt1 < 30.0, dt1
+    assert bool((x.float() == 3.0).all())                            # the residual stream is not written
     dt2 = _timed(call)
     assert dt2 < 1.0, dt2
