@@ -383,65 +383,119 @@ __device__ __forceinline__ void gv_load_x(const __nv_bfloat16 *xr, int k0, int K
 // The activation pre-norm of GemvArgs: scale[t] = rsqrt(mean(x[t]^2) + eps)
 // for the launch's tokens, every CTA the same value (thread i adds elements
 // i, i + blockDim, ... in order, then a fixed tree).  All threads call it.
-// The all-reduce of GemvArgs (ar_*), run by every CTA before the norm:
-// returns false (and records CBQ_FLAG_TIMEOUT) when a rank's rows did not
-// arrive within the bound, or an earlier wait of this run already gave up.
-template <typename XT, int TB>
-__device__ __forceinline__ bool gv_allreduce_in(const GemvArgs &a, int *late) {
-    const int tid = threadIdx.x;
-    if (tid == 0)
-        *late = (a.status && (*(volatile uint32_t *)(a.status + CBQ_STATUS_FLAGS) & CBQ_FLAG_TIMEOUT)) ? 1 : 0;
-    __syncthreads();
-    if (!*late && tid < a.ar_world) {
-        const uint32_t want = *a.ar_epoch * a.ar_expect;
-        const uint64_t t0 = global_timer_ns();
-        while (true) {
-            uint32_t c;
-            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(c) : "l"(a.ar_counts + tid) : "memory");
-            if ((int32_t)(c - want) >= 0) break;
-            if (global_timer_ns() - t0 > kWaitNs) {
-                *late = 1;
-                break;
-            }
-            __nanosleep(64);
+// Eight consecutive activations as fp32 (k0 a multiple of 8; 16-byte
+// aligned rows): one or two 16-byte loads, L2-coherent when `coherent`
+// (values written earlier in the same launch).
+template <typename XT>
+__device__ __forceinline__ void gv_ld8(const XT *p, bool coherent, float (&v)[8]) {
+    if constexpr (std::is_same<XT, float>::value) {
+        const float4 *q = reinterpret_cast<const float4 *>(p);
+        const float4 a = coherent ? __ldcg(q) : __ldg(q), b = coherent ? __ldcg(q + 1) : __ldg(q + 1);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+        const uint4 *q = reinterpret_cast<const uint4 *>(p);
+        const uint4 f = coherent ? __ldcg(q) : __ldg(q);
+        const uint32_t u[4] = {f.x, f.y, f.z, f.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+            v[2 * h] = __uint_as_float(u[h] << 16);
+            v[2 * h + 1] = __uint_as_float(u[h] & 0xffff0000u);
         }
     }
-    __syncthreads();
-    if (*late) {
-        if (tid == 0 && blockIdx.x == 0) report(a.status, CBQ_FLAG_TIMEOUT, 0u);
-        return false;
-    }
-    __threadfence_system();
-    const XT *slots = static_cast<const XT *>(a.ar_slots);
-    const XT *res = static_cast<const XT *>(a.ar_resid);
-    XT *xo = const_cast<XT *>(static_cast<const XT *>(a.x));
-    for (int t = 0; t < a.ntok; ++t) {
-        for (int k = tid; k < a.K; k += kGvWarps * 32) {
-            float sum = 0.f;
-            for (int p = 0; p < a.ar_world; ++p)
-                sum += to_f32<XT>(__ldcg(slots + ((int64_t)p * a.ntok + t) * a.K + k));
-            const float v = to_f32<XT>(from_f32<XT>(to_f32<XT>(res[(a.t0 + t) * a.ldx + k]) +
-                                                     to_f32<XT>(from_f32<XT>(sum))));
-            xo[(a.t0 + t) * a.ldx + k] = from_f32<XT>(v);
-        }
-    }
-    __syncthreads();                                       // this CTA's x rows, before it reads them
-    return true;
 }
 
+template <typename XT>
+__device__ __forceinline__ void gv_st8(XT *p, const float (&v)[8]) {
+    if constexpr (std::is_same<XT, float>::value) {
+        float4 *q = reinterpret_cast<float4 *>(p);
+        q[0] = make_float4(v[0], v[1], v[2], v[3]);
+        q[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else {
+        uint32_t u[4];
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+            const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(v[2 * h]));
+            const uint32_t hi = __bfloat16_as_ushort(__float2bfloat16_rn(v[2 * h + 1]));
+            u[h] = lo | (hi << 16);
+        }
+        *reinterpret_cast<uint4 *>(p) = make_uint4(u[0], u[1], u[2], u[3]);
+    }
+}
+
+// The launch's prologue on its activations (GemvArgs ar_* / pn_*), run by
+// every thread of every CTA after pdl_wait:
+//   * ar_on: wait (bounded) until every rank's partial rows have arrived,
+//     then x[t] = round(ar_resid[t] + round(sum_s slot_s[t])) in rank order,
+//     written to a.x (every CTA writes the same values);
+//   * pn_on: scale[t] = rsqrt(mean(x[t]^2) + eps) of the (new) x rows.
+// Thread i takes the 8-element chunks i, i + blockDim, ... of a row, all
+// loads of a chunk issued together, then the warps' sums are added in warp
+// order, so every CTA computes the same scales.  Returns false when the wait
+// gave up (CBQ_FLAG_TIMEOUT recorded) or an earlier wait of this run had.
 template <typename XT, int TB>
-__device__ __forceinline__ void gv_prenorm_scales(const GemvArgs &a, float (&scale)[TB], float *red) {
-    const XT *x = static_cast<const XT *>(a.x);
+__device__ __forceinline__ bool gv_prologue(const GemvArgs &a, float (&scale)[TB], float *red, int *late) {
+    constexpr int NT = kGvWarps * 32;
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    if (a.ar_on) {
+        if (tid == 0)
+            *late = (a.status && (*(volatile uint32_t *)(a.status + CBQ_STATUS_FLAGS) & CBQ_FLAG_TIMEOUT)) ? 1 : 0;
+        __syncthreads();
+        if (!*late && tid < a.ar_world) {
+            const uint32_t want = *a.ar_epoch * a.ar_expect;
+            const uint64_t t0 = global_timer_ns();
+            while (true) {
+                uint32_t c;
+                asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(c) : "l"(a.ar_counts + tid) : "memory");
+                if ((int32_t)(c - want) >= 0) break;
+                if (global_timer_ns() - t0 > kWaitNs) {
+                    *late = 1;
+                    break;
+                }
+                __nanosleep(32);
+            }
+        }
+        __syncthreads();
+        if (*late) {
+            if (tid == 0 && blockIdx.x == 0) report(a.status, CBQ_FLAG_TIMEOUT, 0u);
+            return false;
+        }
+        __threadfence_system();
+    }
+    const XT *slots = static_cast<const XT *>(a.ar_slots);
+    const XT *res = static_cast<const XT *>(a.ar_resid);
+    XT *x = const_cast<XT *>(static_cast<const XT *>(a.x));
     for (int t = 0; t < TB; ++t) {
         float ss = 0.f;
         if (t < a.ntok) {
-            const XT *xr = x + (a.t0 + t) * a.ldx;
-            for (int k = tid; k < a.K; k += kGvWarps * 32) {
-                const float v = to_f32<XT>(xr[k]);
-                ss = fmaf(v, v, ss);
+            const int64_t row = (a.t0 + t) * a.ldx;
+            for (int k0 = tid * 8; k0 < a.K; k0 += NT * 8) {
+                float v[8];
+                if (a.ar_on) {
+                    float r[8], sum[8], sp[kGvMaxPeers][8];
+                    gv_ld8<XT>(res + row + k0, false, r);
+#pragma unroll
+                    for (int p = 0; p < kGvMaxPeers; ++p)
+                        if (p < a.ar_world) gv_ld8<XT>(slots + ((int64_t)p * a.ntok + t) * a.K + k0, true, sp[p]);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) sum[e] = 0.f;
+#pragma unroll
+                    for (int p = 0; p < kGvMaxPeers; ++p)
+                        if (p < a.ar_world) {
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) sum[e] += sp[p][e];
+                        }
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        v[e] = to_f32<XT>(from_f32<XT>(r[e] + to_f32<XT>(from_f32<XT>(sum[e]))));
+                    gv_st8<XT>(x + row + k0, v);
+                } else {
+                    gv_ld8<XT>(x + row + k0, false, v);
+                }
+#pragma unroll
+                for (int e = 0; e < 8; ++e) ss = fmaf(v[e], v[e], ss);
             }
         }
+        if (!a.pn_on) continue;
         ss = warp_sum(ss);
         if (lane == 0) red[w] = ss;
         __syncthreads();
@@ -451,9 +505,11 @@ __device__ __forceinline__ void gv_prenorm_scales(const GemvArgs &a, float (&sca
         scale[t] = rsqrtf(tot / (float)a.K + a.pn_eps);
         __syncthreads();                                   // red[] reuse
     }
+    if (a.ar_on) __syncthreads();                           // this CTA's x rows, before it reads them
+    return true;
 }
 
-// Normalise NF loaded activations starting at k0 (see gv_prenorm_scales).
+// Normalise NF loaded activations starting at k0 (see gv_prologue).
 template <typename XT, int NF>
 __device__ __forceinline__ void gv_prenorm_apply(float (&v)[NF], float scale, const float *w, int k0, int K) {
     if (k0 >= K) return;
@@ -466,6 +522,24 @@ __device__ __forceinline__ void gv_prenorm_apply(float (&v)[NF], float scale, co
         float y = rnd(v[i] * scale);
         if (w) y = rnd(__ldg(w + k0 + i) * y);
         v[i] = y;
+    }
+}
+
+// gv_load_x for activations written earlier in the same launch (the
+// all-reduce prologue): loads that read L2, not the read-only path.
+template <int NF, typename XT>
+__device__ __forceinline__ void gv_load_x_cg(const XT *xr, int k0, int K, float (&v)[NF]) {
+    if (k0 < K) {
+#pragma unroll
+        for (int q = 0; q < NF / 8; ++q) {
+            float e[8];
+            gv_ld8<XT>(xr + k0 + 8 * q, true, e);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[8 * q + i] = e[i];
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < NF; ++i) v[i] = 0.f;
     }
 }
 
@@ -564,14 +638,10 @@ __global__ void __launch_bounds__(kGvWarps * 32, 1) k_gemv_fixed(const GemvArgs 
     float pn_scale[TB];
 #pragma unroll
     for (int t = 0; t < TB; ++t) pn_scale[t] = 1.f;
-    bool ar_ok = true;
-    if (a.ar_on) {
-        __shared__ int ar_late;
-        ar_ok = gv_allreduce_in<XT, TB>(a, &ar_late);
-    }
-    if (a.pn_on && ar_ok) {
+    if (a.ar_on || a.pn_on) {
         __shared__ float pn_red[kGvWarps];
-        gv_prenorm_scales<XT, TB>(a, pn_scale, pn_red);
+        __shared__ int ar_late;
+        gv_prologue<XT, TB>(a, pn_scale, pn_red, &ar_late);
     }
 
     const uint32_t cb_base = smem_u32(cbs);
@@ -600,7 +670,8 @@ __global__ void __launch_bounds__(kGvWarps * 32, 1) k_gemv_fixed(const GemvArgs 
 #pragma unroll
             for (int t = 0; t < TB; ++t) {
                 if (t < a.ntok) {
-                    gv_load_x<NF>(x + (a.t0 + t) * a.ldx, k0, K, xr[t]);
+                    if (a.ar_on) gv_load_x_cg<NF>(x + (a.t0 + t) * a.ldx, k0, K, xr[t]);
+                    else gv_load_x<NF>(x + (a.t0 + t) * a.ldx, k0, K, xr[t]);
                     if (a.pn_on) gv_prenorm_apply<XT, NF>(xr[t], pn_scale[t], a.pn_w, k0, K);
                 } else {
 #pragma unroll
