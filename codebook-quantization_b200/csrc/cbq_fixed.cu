@@ -159,7 +159,8 @@ struct GemvPlan {
     size_t smem = 0;
 };
 
-bool plan_gemv(int64_t M, int64_t K, int bits, int64_t C, int64_t T, GemvPlan &p, bool even_rows = false) {
+bool plan_gemv(int64_t M, int64_t K, int bits, int64_t C, int64_t T, GemvPlan &p, bool even_rows = false,
+               size_t xs_bytes = 0) {
     if (T < 1 || T > 2 || K <= 0 || K % 128 != 0 || K > (1 << 20) || M <= 0 || M >= (1ll << 31))
         return false;
     const int64_t sms = cbq_host::sm_count();
@@ -171,7 +172,8 @@ bool plan_gemv(int64_t M, int64_t K, int bits, int64_t C, int64_t T, GemvPlan &p
     const int nseg = (int)((K + 32 * nf - 1) / (32 * nf));
     const int64_t NP = (bits <= 14) ? std::max<int64_t>(C, 1ll << bits) : C;
     const size_t budget = (size_t)cbq_host::max_smem_optin();
-    const size_t fixed = kGvBarBytes + gemv_part_bytes((int)rows, nseg, (int)T) + gemv_ring_bytes(bits, nf);
+    const size_t fixed = kGvBarBytes + gemv_part_bytes((int)rows, nseg, (int)T) + gemv_ring_bytes(bits, nf) +
+                         a128(xs_bytes);
     if (fixed + a128((size_t)NP * 4) > budget) return false;
     int64_t H = (int64_t)((budget - fixed - 128 - (size_t)NP * 4) / 124);
     H = std::min<int64_t>(H, C);
@@ -349,7 +351,8 @@ int linear_fixed_multi_impl(const void *x_dev, int x_dtype, int64_t T, int64_t l
     const int xbytes = x_dtype == CBQ_BF16 ? 2 : 4;
     if ((reinterpret_cast<uintptr_t>(x_dev) & 15) != 0 || (ldx * xbytes) % 16 != 0) return CBQ_ERR_UNSUPPORTED;
     GemvPlan g;
-    if (!plan_gemv(Mt, K, bits, C, T, g, epilogue == CBQ_EPI_SILU_MUL)) return CBQ_ERR_UNSUPPORTED;
+    const size_t xs_bytes = ar ? (size_t)T * K * xbytes : 0;     // the all-reduced activations in shared memory
+    if (!plan_gemv(Mt, K, bits, C, T, g, epilogue == CBQ_EPI_SILU_MUL, xs_bytes)) return CBQ_ERR_UNSUPPORTED;
     GemvArgs a{};
     a.x = x_dev; a.ldx = ldx; a.t0 = 0; a.ntok = (int)T; a.codebook = codebook_dev;
     a.C = (int)C; a.M = (int)Mt; a.K = (int)K; a.nseg = g.nseg; a.rows_per_cta = g.rows_per_cta;

@@ -426,14 +426,16 @@ __device__ __forceinline__ void gv_st8(XT *p, const float (&v)[8]) {
 // every thread of every CTA after pdl_wait:
 //   * ar_on: wait (bounded) until every rank's partial rows have arrived,
 //     then x[t] = round(ar_resid[t] + round(sum_s slot_s[t])) in rank order,
-//     written to a.x (every CTA writes the same values);
+//     kept in shared memory (xs, [TB][K]) for this CTA's loads and written to
+//     a.x by CTA 0 only (the residual stream for later launches);
 //   * pn_on: scale[t] = rsqrt(mean(x[t]^2) + eps) of the (new) x rows.
 // Thread i takes the 8-element chunks i, i + blockDim, ... of a row, all
 // loads of a chunk issued together, then the warps' sums are added in warp
 // order, so every CTA computes the same scales.  Returns false when the wait
 // gave up (CBQ_FLAG_TIMEOUT recorded) or an earlier wait of this run had.
 template <typename XT, int TB>
-__device__ __forceinline__ bool gv_prologue(const GemvArgs &a, float (&scale)[TB], float *red, int *late) {
+__device__ __forceinline__ bool gv_prologue(const GemvArgs &a, float (&scale)[TB], float *red, int *late,
+                                            XT *xs) {
     constexpr int NT = kGvWarps * 32;
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     if (a.ar_on) {
@@ -459,7 +461,8 @@ __device__ __forceinline__ bool gv_prologue(const GemvArgs &a, float (&scale)[TB
             if (tid == 0 && blockIdx.x == 0) report(a.status, CBQ_FLAG_TIMEOUT, 0u);
             return false;
         }
-        __threadfence_system();
+        // the pollers' system-scope acquire loads, then the CTA barrier, order
+        // every thread's reads of the slots after the ranks' releases
     }
     const XT *slots = static_cast<const XT *>(a.ar_slots);
     const XT *res = static_cast<const XT *>(a.ar_resid);
@@ -487,7 +490,8 @@ __device__ __forceinline__ bool gv_prologue(const GemvArgs &a, float (&scale)[TB
 #pragma unroll
                     for (int e = 0; e < 8; ++e)
                         v[e] = to_f32<XT>(from_f32<XT>(r[e] + to_f32<XT>(from_f32<XT>(sum[e]))));
-                    gv_st8<XT>(x + row + k0, v);
+                    gv_st8<XT>(xs + (int64_t)t * a.K + k0, v);
+                    if (blockIdx.x == 0) gv_st8<XT>(x + row + k0, v);
                 } else {
                     gv_ld8<XT>(x + row + k0, false, v);
                 }
@@ -505,7 +509,7 @@ __device__ __forceinline__ bool gv_prologue(const GemvArgs &a, float (&scale)[TB
         scale[t] = rsqrtf(tot / (float)a.K + a.pn_eps);
         __syncthreads();                                   // red[] reuse
     }
-    if (a.ar_on) __syncthreads();                           // this CTA's x rows, before it reads them
+    if (a.ar_on) __syncthreads();                           // xs complete before any warp reads it
     return true;
 }
 
@@ -525,17 +529,27 @@ __device__ __forceinline__ void gv_prenorm_apply(float (&v)[NF], float scale, co
     }
 }
 
-// gv_load_x for activations written earlier in the same launch (the
-// all-reduce prologue): loads that read L2, not the read-only path.
+// gv_load_x from the shared-memory copy of the activations the all-reduce
+// prologue formed (xs row, 16-byte aligned).
 template <int NF, typename XT>
-__device__ __forceinline__ void gv_load_x_cg(const XT *xr, int k0, int K, float (&v)[NF]) {
+__device__ __forceinline__ void gv_load_x_smem(const XT *xr, int k0, int K, float (&v)[NF]) {
     if (k0 < K) {
 #pragma unroll
         for (int q = 0; q < NF / 8; ++q) {
-            float e[8];
-            gv_ld8<XT>(xr + k0 + 8 * q, true, e);
+            if constexpr (std::is_same<XT, float>::value) {
+                const float4 a = reinterpret_cast<const float4 *>(xr + k0)[2 * q];
+                const float4 b = reinterpret_cast<const float4 *>(xr + k0)[2 * q + 1];
+                v[8 * q] = a.x; v[8 * q + 1] = a.y; v[8 * q + 2] = a.z; v[8 * q + 3] = a.w;
+                v[8 * q + 4] = b.x; v[8 * q + 5] = b.y; v[8 * q + 6] = b.z; v[8 * q + 7] = b.w;
+            } else {
+                const uint4 f = reinterpret_cast<const uint4 *>(xr + k0)[q];
+                const uint32_t u[4] = {f.x, f.y, f.z, f.w};
 #pragma unroll
-            for (int i = 0; i < 8; ++i) v[8 * q + i] = e[i];
+                for (int h = 0; h < 4; ++h) {
+                    v[8 * q + 2 * h] = __uint_as_float(u[h] << 16);
+                    v[8 * q + 2 * h + 1] = __uint_as_float(u[h] & 0xffff0000u);
+                }
+            }
         }
     } else {
 #pragma unroll
@@ -560,6 +574,8 @@ __global__ void __launch_bounds__(kGvWarps * 32, 1) k_gemv_fixed(const GemvArgs 
     float *part = reinterpret_cast<float *>(smem + kGvBarBytes);
     uint8_t *cbs = smem + kGvBarBytes + gemv_part_bytes(a.rows_per_cta, nseg, TB);
     uint8_t *ring = cbs + gemv_cb_bytes(a.H, a.NP) + (size_t)warp * kGvSlots * kSegBytes;
+    // ar_on: the all-reduced activations [TB][K] after the rings
+    XT *xsm = reinterpret_cast<XT *>(cbs + gemv_cb_bytes(a.H, a.NP) + gemv_ring_bytes(BITS, NF));
 
     // this warp's units: u = s * nrows + rl (segment-major)
     const int U = nrows * nseg;
@@ -641,7 +657,7 @@ __global__ void __launch_bounds__(kGvWarps * 32, 1) k_gemv_fixed(const GemvArgs 
     if (a.ar_on || a.pn_on) {
         __shared__ float pn_red[kGvWarps];
         __shared__ int ar_late;
-        gv_prologue<XT, TB>(a, pn_scale, pn_red, &ar_late);
+        gv_prologue<XT, TB>(a, pn_scale, pn_red, &ar_late, xsm);
     }
 
     const uint32_t cb_base = smem_u32(cbs);
@@ -670,7 +686,7 @@ __global__ void __launch_bounds__(kGvWarps * 32, 1) k_gemv_fixed(const GemvArgs 
 #pragma unroll
             for (int t = 0; t < TB; ++t) {
                 if (t < a.ntok) {
-                    if (a.ar_on) gv_load_x_cg<NF>(x + (a.t0 + t) * a.ldx, k0, K, xr[t]);
+                    if (a.ar_on) gv_load_x_smem<NF, XT>(xsm + (int64_t)t * K, k0, K, xr[t]);
                     else gv_load_x<NF>(x + (a.t0 + t) * a.ldx, k0, K, xr[t]);
                     if (a.pn_on) gv_prenorm_apply<XT, NF>(xr[t], pn_scale[t], a.pn_w, k0, K);
                 } else {
