@@ -39,6 +39,8 @@ SIGNATURES = {
     "cbq_linear_fixed_multi_allreduce_norm": (_INT, [_P, _INT, _I64, _I64, _INT, _P, _P, _P, _P, _I64, _INT, _I64,
                                                      _P, _P, _P, _P, _INT, _INT, _P, ct.c_float, _INT, _P, _P, _P,
                                                      _P, _I64, _P, _P]),
+    "cbq_linear_fixed_peer_flagged": (_INT, [_P, _INT, _I64, _I64, _P, _I64, _P, _I64, _INT, _I64, _I64, _P, _INT,
+                                             _P, _P, _I64, _INT, _P]),
     "cbq_linear_fixed_peer": (_INT, [_P, _INT, _I64, _I64, _P, _I64, _P, _I64, _INT, _I64, _I64, _P, _INT,
                                      _P, _P, _I64, _INT, _P]),
     "cbq_linear_fixed_peer_norm": (_INT, [_P, _INT, _I64, _I64, _P, _I64, _P, _I64, _INT, _I64, _I64, _P, _INT,

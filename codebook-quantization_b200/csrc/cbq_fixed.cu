@@ -365,7 +365,7 @@ int linear_fixed_multi_impl(const void *x_dev, int x_dtype, int64_t T, int64_t l
     a.pn_on = pn_on; a.pn_w = pn_w; a.pn_eps = pn_eps;
     if (ar) {
         a.ar_on = 1; a.ar_world = ar->ar_world; a.ar_slots = ar->ar_slots; a.ar_counts = ar->ar_counts;
-        a.ar_epoch = ar->ar_epoch; a.ar_expect = ar->ar_expect; a.ar_resid = ar->ar_resid;
+        a.ar_epoch = ar->ar_epoch; a.ar_expect = ar->ar_expect; a.ar_resid = ar->ar_resid; a.ar_ll = ar->ar_ll;
         a.status = ar->status;
     }
     return launch_gemv(bits, (int)T, g.nf, x_dtype == CBQ_BF16, a, g.smem, g.grid,
@@ -403,12 +403,17 @@ extern "C" int cbq_linear_fixed_multi_allreduce_norm(
     int out_dtype, int epilogue, const float *norm_weight_dev, float eps, int world, const void *resid_in_dev,
     const void *local_slots_dev, const uint32_t *local_counts_dev, const uint32_t *epoch_dev, int64_t expect,
     uint32_t *status_dev, void *stream) {
-    if (world < 1 || world > kGvMaxPeers || !resid_in_dev || !local_slots_dev || !local_counts_dev || !epoch_dev ||
-        expect < 1 || expect > 0xffffffffll || resid_in_dev == x_dev)
+    // local_counts_dev NULL: the slots are in the flagged form
+    // (cbq_linear_fixed_peer_flagged) and expect is unused
+    const bool ll = local_counts_dev == nullptr;
+    if (world < 1 || world > kGvMaxPeers || !resid_in_dev || !local_slots_dev || !epoch_dev ||
+        (!ll && (expect < 1 || expect > 0xffffffffll)) || resid_in_dev == x_dev)
+        return CBQ_ERR_ARG;
+    if (ll && ((reinterpret_cast<uintptr_t>(local_slots_dev) & 7) || (x_dtype == CBQ_BF16 && K % 2)))
         return CBQ_ERR_ARG;
     GemvArgs ar{};
     ar.ar_world = world; ar.ar_slots = local_slots_dev; ar.ar_counts = local_counts_dev; ar.ar_epoch = epoch_dev;
-    ar.ar_expect = (uint32_t)expect; ar.ar_resid = resid_in_dev; ar.status = status_dev;
+    ar.ar_expect = (uint32_t)expect; ar.ar_resid = resid_in_dev; ar.status = status_dev; ar.ar_ll = ll;
     return linear_fixed_multi_impl(x_dev, x_dtype, T, ldx, nmat, packed_dev, packed_bytes, M, codebook_dev, C,
                                    bits, K, bias_dev, out_dev, ldo, resid_dev, out_dtype, epilogue, 1,
                                    norm_weight_dev, eps, stream, &ar);
@@ -420,19 +425,23 @@ namespace {
 int peer_args(const void *x_dev, int x_dtype, int64_t T, int64_t ldx, const uint8_t *packed_dev,
               int64_t packed_bytes, const float *codebook_dev, int64_t C, int bits, int64_t M, int64_t K,
               const float *bias_dev, int world, void *const *slot_dev, uint32_t *const *count_dev, int64_t ldo,
-              int out_dtype, GemvArgs &a, GemvPlan &g) {
-    if (world < 1 || world > kGvMaxPeers || !slot_dev || !count_dev) return CBQ_ERR_ARG;
+              int out_dtype, GemvArgs &a, GemvPlan &g, const uint32_t *ll_epoch = nullptr) {
+    if (world < 1 || world > kGvMaxPeers || !slot_dev || (!count_dev && !ll_epoch)) return CBQ_ERR_ARG;
+    // flagged bf16 slots hold row pairs: even M and an even row split
+    const bool pairs = ll_epoch && out_dtype == CBQ_BF16;
+    if (pairs && (M % 2 || ldo % 2)) return CBQ_ERR_UNSUPPORTED;
     if (T < 1 || M < 1 || K < 1 || bits < 1 || bits > 16 || C < 1 || C > 65536 || ldo < M) return CBQ_ERR_ARG;
     if ((x_dtype != CBQ_F32 && x_dtype != CBQ_BF16) || (out_dtype != CBQ_F32 && out_dtype != CBQ_BF16))
         return CBQ_ERR_ARG;
     if (!x_dev || !packed_dev || !codebook_dev || ldx < K) return CBQ_ERR_ARG;
     if (packed_bytes < cbq_fixed_stream_bytes(M, K, bits)) return CBQ_ERR_ARG;
     for (int p = 0; p < world; ++p)
-        if (!slot_dev[p] || !count_dev[p]) return CBQ_ERR_ARG;
+        if (!slot_dev[p] || (!ll_epoch && !count_dev[p]) || (ll_epoch && (reinterpret_cast<uintptr_t>(slot_dev[p]) & 7)))
+            return CBQ_ERR_ARG;
     const int xbytes = x_dtype == CBQ_BF16 ? 2 : 4;
     if ((reinterpret_cast<uintptr_t>(x_dev) & 15) || (ldx * xbytes) % 16 || (reinterpret_cast<uintptr_t>(packed_dev) & 15))
         return CBQ_ERR_UNSUPPORTED;
-    if (!plan_gemv(M, K, bits, C, T, g)) return CBQ_ERR_UNSUPPORTED;
+    if (!plan_gemv(M, K, bits, C, T, g, pairs)) return CBQ_ERR_UNSUPPORTED;
     a = GemvArgs{};
     a.x = x_dev; a.ldx = ldx; a.t0 = 0; a.ntok = (int)T; a.codebook = codebook_dev;
     a.C = (int)C; a.M = (int)M; a.K = (int)K; a.nseg = g.nseg; a.rows_per_cta = g.rows_per_cta;
@@ -441,14 +450,30 @@ int peer_args(const void *x_dev, int x_dtype, int64_t T, int64_t ldx, const uint
     a.out_bf16 = out_dtype == CBQ_BF16;
     a.H = g.H; a.NP = g.NP; a.m128 = 128u; a.m4 = 4u; a.status = nullptr;
     a.peers.world = world;
+    a.peers.ll_epoch = ll_epoch;
     for (int p = 0; p < world; ++p) {
         a.peers.slot[p] = slot_dev[p];
-        a.peers.count[p] = count_dev[p];
+        a.peers.count[p] = count_dev ? count_dev[p] : nullptr;
     }
     return CBQ_OK;
 }
 
 }  // namespace
+
+extern "C" int cbq_linear_fixed_peer_flagged(const void *x_dev, int x_dtype, int64_t T, int64_t ldx,
+                                             const uint8_t *packed_dev, int64_t packed_bytes,
+                                             const float *codebook_dev, int64_t C, int bits, int64_t M, int64_t K,
+                                             const float *bias_dev, int world, void *const *slot_dev,
+                                             const uint32_t *epoch_dev, int64_t ldo, int out_dtype, void *stream) {
+    if (!epoch_dev) return CBQ_ERR_ARG;
+    GemvArgs a;
+    GemvPlan g;
+    const int rc = peer_args(x_dev, x_dtype, T, ldx, packed_dev, packed_bytes, codebook_dev, C, bits, M, K, bias_dev,
+                             world, slot_dev, nullptr, ldo, out_dtype, a, g, epoch_dev);
+    if (rc != CBQ_OK) return rc;
+    return launch_gemv(bits, (int)T, g.nf, x_dtype == CBQ_BF16, a, g.smem, g.grid,
+                       static_cast<cudaStream_t>(stream));
+}
 
 extern "C" int cbq_linear_fixed_peer(const void *x_dev, int x_dtype, int64_t T, int64_t ldx,
                                      const uint8_t *packed_dev, int64_t packed_bytes, const float *codebook_dev,

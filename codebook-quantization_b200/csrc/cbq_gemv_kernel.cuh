@@ -85,7 +85,22 @@ struct GemvPeers {
     void *slot[kGvMaxPeers];          // rank p's slot for this rank, [T, ldo] in the output dtype
     uint32_t *count[kGvMaxPeers];     // rank p's arrival counter for this rank
     int world;
+    // Flagged form (counts unused): every 64-bit slot word carries 32 bits of
+    // data and the step's epoch in its high half, stored with one relaxed
+    // system-scope 64-bit store, so a reader that sees the epoch sees the
+    // data of the same store (no fence, no counter).  bf16: word t * ldo/2 +
+    // row/2 holds rows (row, row + 1); fp32: word t * ldo + row.
+    const uint32_t *ll_epoch;
 };
+
+__device__ __forceinline__ void st_relaxed_sys_u64(void *p, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const void *p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
 
 // Optional RMSNorm of the launch's updated rows (kEpiResidual with one
 // matrix, or kEpiPeer), done by the CTA that finishes last: every CTA fences
@@ -142,6 +157,7 @@ struct GemvArgs {
     // not ar_resid), from where the launch loads it.
     int ar_on;
     int ar_world;
+    int ar_ll;           // the slots are in the flagged form (GemvPeers::ll_epoch; ar_counts unused)
     const void *ar_slots;
     const uint32_t *ar_counts;
     const uint32_t *ar_epoch;
@@ -422,6 +438,52 @@ __device__ __forceinline__ void gv_st8(XT *p, const float (&v)[8]) {
     }
 }
 
+// Eight activations k0..k0+7 of token t from every rank's flagged slot
+// (GemvPeers::ll_epoch): the 64-bit words are read until each carries this
+// step's epoch (bounded; on giving up sets *late, records CBQ_FLAG_TIMEOUT
+// and returns false).  Slot p of the consumer's buffer is ar_slots + p *
+// ntok * K words (fp32) or K/2 words (bf16) per token.
+template <typename XT>
+__device__ __forceinline__ bool gv_ll_read8(const GemvArgs &a, int t, int k0, float (&sp)[kGvMaxPeers][8],
+                                            int *late) {
+    constexpr bool kBf = !std::is_same<XT, float>::value;
+    constexpr int NWD = kBf ? 4 : 8;                        // words per 8 activations
+    const int64_t per_tok = kBf ? a.K / 2 : a.K;
+    const uint64_t *base = static_cast<const uint64_t *>(a.ar_slots);
+    const uint32_t ep = *a.ar_epoch;
+    uint64_t t0 = 0;
+    for (int p = 0; p < a.ar_world; ++p) {
+        const uint64_t *w = base + ((int64_t)p * a.ntok + t) * per_tok + (kBf ? k0 / 2 : k0);
+        uint64_t v[NWD];
+        while (true) {
+#pragma unroll
+            for (int i = 0; i < NWD; ++i) v[i] = ld_relaxed_sys_u64(w + i);
+            bool ok = true;
+#pragma unroll
+            for (int i = 0; i < NWD; ++i) ok &= (uint32_t)(v[i] >> 32) == ep;
+            if (ok) break;
+            if (*(volatile int *)late) return false;         // this CTA, or an earlier call, gave up
+            if (t0 == 0) t0 = global_timer_ns();
+            else if (global_timer_ns() - t0 > kWaitNs) {
+                if (atomicExch(late, 1) == 0) report(a.status, CBQ_FLAG_TIMEOUT, 0u);
+                return false;
+            }
+            __nanosleep(32);
+        }
+#pragma unroll
+        for (int i = 0; i < NWD; ++i) {
+            const uint32_t d = (uint32_t)v[i];
+            if (kBf) {
+                sp[p][2 * i] = __uint_as_float(d << 16);
+                sp[p][2 * i + 1] = __uint_as_float(d & 0xffff0000u);
+            } else {
+                sp[p][i] = __uint_as_float(d);
+            }
+        }
+    }
+    return true;
+}
+
 // The launch's prologue on its activations (GemvArgs ar_* / pn_*), run by
 // every thread of every CTA after pdl_wait:
 //   * ar_on: wait (bounded) until every rank's partial rows have arrived,
@@ -442,7 +504,7 @@ __device__ __forceinline__ bool gv_prologue(const GemvArgs &a, float (&scale)[TB
         if (tid == 0)
             *late = (a.status && (*(volatile uint32_t *)(a.status + CBQ_STATUS_FLAGS) & CBQ_FLAG_TIMEOUT)) ? 1 : 0;
         __syncthreads();
-        if (!*late && tid < a.ar_world) {
+        if (!*late && tid < a.ar_world && !a.ar_ll) {
             const uint32_t want = *a.ar_epoch * a.ar_expect;
             const uint64_t t0 = global_timer_ns();
             while (true) {
@@ -476,9 +538,21 @@ __device__ __forceinline__ bool gv_prologue(const GemvArgs &a, float (&scale)[TB
                 if (a.ar_on) {
                     float r[8], sum[8], sp[kGvMaxPeers][8];
                     gv_ld8<XT>(res + row + k0, false, r);
+                    if (a.ar_ll) {
+                        // on giving up the values are zeros; every thread still
+                        // reaches the barriers below, and the call reports it
+                        if (!gv_ll_read8<XT>(a, t, k0, sp, late)) {
 #pragma unroll
-                    for (int p = 0; p < kGvMaxPeers; ++p)
-                        if (p < a.ar_world) gv_ld8<XT>(slots + ((int64_t)p * a.ntok + t) * a.K + k0, true, sp[p]);
+                            for (int p = 0; p < kGvMaxPeers; ++p)
+#pragma unroll
+                                for (int e = 0; e < 8; ++e) sp[p][e] = 0.f;
+                        }
+                    } else {
+#pragma unroll
+                        for (int p = 0; p < kGvMaxPeers; ++p)
+                            if (p < a.ar_world)
+                                gv_ld8<XT>(slots + ((int64_t)p * a.ntok + t) * a.K + k0, true, sp[p]);
+                    }
 #pragma unroll
                     for (int e = 0; e < 8; ++e) sum[e] = 0.f;
 #pragma unroll
@@ -510,7 +584,7 @@ __device__ __forceinline__ bool gv_prologue(const GemvArgs &a, float (&scale)[TB
         __syncthreads();                                   // red[] reuse
     }
     if (a.ar_on) __syncthreads();                           // xs complete before any warp reads it
-    return true;
+    return !(a.ar_on && *(volatile int *)late);
 }
 
 // Normalise NF loaded activations starting at k0 (see gv_prologue).
@@ -793,6 +867,33 @@ __global__ void __launch_bounds__(kGvWarps * 32, 1) k_gemv_fixed(const GemvArgs 
                 const float gv = rnd(seg_sum(r, t) + bg), uv = rnd(seg_sum(r + 1, t) + bu);
                 const float sv = rnd(gv / (1.0f + expf(-gv)));
                 store(g, (a.t0 + t) * g.ldo + row, sv * uv);
+            }
+        }
+    } else if (a.epi == kEpiPeer && a.peers.ll_epoch) {
+        const GemvMat &mt = a.mat[0];
+        const uint64_t ep = (uint64_t)*a.peers.ll_epoch << 32;
+        if (a.out_bf16) {                                  // row pairs (rows_per_cta and M are even)
+            for (int r = 2 * tid; r + 1 < nrows; r += 2 * kGvWarps * 32) {
+                const int64_t row = m0 + r;
+                const float b0 = mt.bias ? mt.bias[row] : 0.f, b1 = mt.bias ? mt.bias[row + 1] : 0.f;
+                for (int t = 0; t < a.ntok; ++t) {
+                    const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(seg_sum(r, t) + b0));
+                    const uint32_t hi = __bfloat16_as_ushort(__float2bfloat16_rn(seg_sum(r + 1, t) + b1));
+                    const int64_t w = (a.t0 + t) * (mt.ldo / 2) + row / 2;
+                    for (int p = 0; p < a.peers.world; ++p)
+                        st_relaxed_sys_u64(static_cast<uint64_t *>(a.peers.slot[p]) + w, ep | lo | (hi << 16));
+                }
+            }
+        } else {
+            for (int r = tid; r < nrows; r += kGvWarps * 32) {
+                const int64_t row = m0 + r;
+                const float b = mt.bias ? mt.bias[row] : 0.f;
+                for (int t = 0; t < a.ntok; ++t) {
+                    const int64_t w = (a.t0 + t) * mt.ldo + row;
+                    const uint64_t v = ep | __float_as_uint(seg_sum(r, t) + b);
+                    for (int p = 0; p < a.peers.world; ++p)
+                        st_relaxed_sys_u64(static_cast<uint64_t *>(a.peers.slot[p]) + w, v);
+                }
             }
         }
     } else if (a.epi == kEpiPeer) {

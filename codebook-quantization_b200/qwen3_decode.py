@@ -68,7 +68,12 @@ class _PeerAllReduce:
         if self.slot_bytes % 16:
             raise ValueError("batch * hidden must fill whole 16-byte units")
         data = sites * W * self.slot_bytes
-        total = data + ((sites * W * 4 + 127) // 128) * 128
+        counters = ((sites * W * 4 + 127) // 128) * 128
+        # flagged slots (cbq_linear_fixed_peer_flagged): 64-bit words of 32
+        # data bits + the epoch, two bf16 or one fp32 value per word
+        self.flag_bytes = dec.B * dec.cfg.hidden * (4 if self.elem == 2 else 8)
+        self.flag_off = data + counters
+        total = self.flag_off + sites * W * self.flag_bytes
         self.buf = symm.empty(total, dtype=torch.uint8, device=dec.dev)
         self.buf.zero_()
         self.hdl = symm.rendezvous(self.buf, dec.group)
@@ -77,24 +82,31 @@ class _PeerAllReduce:
         self.data = data
         self.epoch = torch.zeros(1, dtype=torch.int32, device=dec.dev)
         self.status = torch.zeros(4, dtype=torch.int32, device=dec.dev)
-        self.slots, self.counts = [], []
+        self.slots, self.counts, self.flagged = [], [], []
         P = ct.c_void_p
         for i in range(sites):
             self.slots.append((P * W)(*[ptrs[p] + (i * W + r) * self.slot_bytes for p in range(W)]))
             self.counts.append((P * W)(*[ptrs[p] + data + (i * W + r) * 4 for p in range(W)]))
+            self.flagged.append((P * W)(*[ptrs[p] + self.flag_off + (i * W + r) * self.flag_bytes
+                                          for p in range(W)]))
         torch.cuda.synchronize(dec.dev)
         dist.barrier(group=dec.group)
 
     def produce(self, site: int, lin, x):
-        """The row-parallel GEMV whose epilogue stores its partial rows into
-        slot ``rank`` of every rank's buffer for ``site`` and counts them."""
+        """The row-parallel GEMV whose epilogue stores its partial rows, as
+        epoch-flagged words, into slot ``rank`` of every rank's buffer for
+        ``site`` (cbq_linear_fixed_peer_flagged)."""
         dec = self.dec
-        rc = _lib.lib().cbq_linear_fixed_peer(
+        rc = _lib.lib().cbq_linear_fixed_peer_flagged(
             x.data_ptr(), dec.code, dec.B, x.shape[1], lin.packed.data_ptr(), lin.nbytes, lin.codebook.data_ptr(),
-            lin.C, lin.bits, lin.M, lin.K, None, self.W, self.slots[site], self.counts[site], lin.M, dec.code,
+            lin.C, lin.bits, lin.M, lin.K, None, self.W, self.flagged[site], self.epoch.data_ptr(), lin.M, dec.code,
             device_stream(dec.dev))
         if rc != _lib.CBQ_OK:
-            raise _lib.CbqError("cbq_linear_fixed_peer", rc)
+            raise _lib.CbqError("cbq_linear_fixed_peer_flagged", rc)
+
+    def local_flagged(self, site: int) -> int:
+        """This rank's flagged slots of ``site`` (rank s's slot at + s * flag_bytes)."""
+        return self.local + self.flag_off + site * self.W * self.flag_bytes
 
     def run(self, site: int, lin, x):
         dec = self.dec
@@ -369,8 +381,7 @@ class Qwen3Decoder:
         pr = self.peer
         W = pr.W
         src, dst = self.xr[j % 2], self.xr[(j + 1) % 2]
-        ar = (W, src, pr.local + site * W * pr.slot_bytes, pr.local + pr.data + site * W * 4,
-              pr.epoch.data_ptr(), self.cfg.hidden, pr.status.data_ptr())
+        ar = (W, src, pr.local_flagged(site), None, pr.epoch.data_ptr(), self.cfg.hidden, pr.status.data_ptr())
         if not linear_fixed_multi(mats, dst, outs, epilogue, norm=(None, self.cfg.rms_eps), allreduce=ar):
             raise RuntimeError("tensor-parallel all-reduce GEMV: shape not supported by the fused kernel")
         return j + 1

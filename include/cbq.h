@@ -155,7 +155,11 @@ int cbq_linear_fixed_multi_norm(const void *x_dev, int x_dtype, int64_t T, int64
  * (slot s row t at local_slots_dev + (s * T + t) * K elements), writes it to
  * x_dev (the updated residual stream; resid_in_dev is a different buffer,
  * same ldx) and runs the normalised GEMV on it.  One launch replaces the
- * all-reduce consumer, the RMSNorm and the GEMV.  No counterpart in the
+ * all-reduce consumer, the RMSNorm and the GEMV.  With local_counts_dev NULL
+ * the slots are in the flagged form of cbq_linear_fixed_peer_flagged (slot s
+ * at local_slots_dev + s * T * K/2 words for bf16, s * T * K words for fp32;
+ * expect unused): each CTA reads the words until they carry *epoch_dev
+ * (bounded likewise), with no counter and no fence.  No counterpart in the
  * reference (single device). */
 int cbq_linear_fixed_multi_allreduce_norm(
     const void *x_dev, int x_dtype, int64_t T, int64_t ldx, int nmat, const uint8_t *const *packed_dev,
@@ -164,6 +168,20 @@ int cbq_linear_fixed_multi_allreduce_norm(
     int out_dtype, int epilogue, const float *norm_weight_dev, float eps, int world, const void *resid_in_dev,
     const void *local_slots_dev, const uint32_t *local_counts_dev, const uint32_t *epoch_dev, int64_t expect,
     uint32_t *status_dev, void *stream);
+
+/* cbq_linear_fixed_peer with flagged slots instead of counters: every
+ * output is stored into rank p's slot (slot_dev[p], 8-byte aligned) as a
+ * 64-bit word holding 32 bits of data (two bf16 rows (row, row + 1) at word
+ * t * ldo/2 + row/2, or one fp32 row at word t * ldo + row) and *epoch_dev in
+ * its high 32 bits, with one relaxed system-scope store, so the consumer
+ * (cbq_linear_fixed_multi_allreduce_norm with local_counts_dev NULL) knows a
+ * word is this step's by its epoch alone.  bf16 needs even M and ldo (else
+ * CBQ_ERR_UNSUPPORTED).  The epoch grows by one per use of a slot; slots start
+ * zeroed.  No counterpart in the reference (single device). */
+int cbq_linear_fixed_peer_flagged(const void *x_dev, int x_dtype, int64_t T, int64_t ldx, const uint8_t *packed_dev,
+                                  int64_t packed_bytes, const float *codebook_dev, int64_t C, int bits, int64_t M,
+                                  int64_t K, const float *bias_dev, int world, void *const *slot_dev,
+                                  const uint32_t *epoch_dev, int64_t ldo, int out_dtype, void *stream);
 
 /* Tensor-parallel row-parallel layer (o_proj, down_proj), fused with the
  * data movement of its all-reduce: the GEMV of this rank's K-block writes its

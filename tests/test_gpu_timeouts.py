@@ -140,3 +140,30 @@ def test_allreduce_consuming_gemv_wait_runs_out():
     assert bool((x.float() == 3.0).all())                            # the residual stream is not written
     dt2 = _timed(call)
     assert dt2 < 1.0, dt2
+
+
+def test_flagged_slot_read_runs_out():
+    """The flagged-slot form of the consuming GEMV: slot words that never
+    carry the step's epoch make every CTA's read give up within the bound."""
+    dev = need_cuda()
+    world, T, M, K, bits = 2, 1, 256, 512, 13
+    rng = np.random.default_rng(6)
+    idx = rng.integers(0, 1 << bits, size=M * K).astype(np.uint16)
+    cb = torch.from_numpy(rng.standard_normal(1 << bits).astype(np.float32)).to(dev)
+    lin = cbq.GPUAcceleratedLinear("w", cbq.bitpack.pack_any_bits(idx, bits), cb, (M, K), bits, device=dev)
+    resid_in = torch.randn(T, K, device=dev).to(torch.bfloat16)
+    x = torch.full((T, K), 3.0, device=dev).to(torch.bfloat16)
+    slots = torch.zeros(world * T * K * 4, dtype=torch.uint8, device=dev)   # epoch 0 everywhere
+    epoch = torch.ones(1, dtype=torch.int32, device=dev)
+    out = torch.empty(T, M, device=dev, dtype=torch.bfloat16)
+    status = _status(dev)
+    ar = (world, resid_in, slots.data_ptr(), None, epoch.data_ptr(), K, status.data_ptr())
+
+    def call():
+        assert cbq.gpu_accelerated_functions.linear_fixed_multi([lin], x, [out], norm=(None, 1e-6), allreduce=ar)
+    dt1 = _timed(call)
+    st = status.cpu().numpy()
+    assert st[0] & L.FLAG_TIMEOUT, st
+    assert 1.5 < dt1 < 30.0, dt1
+    dt2 = _timed(call)
+    assert dt2 < 1.0, dt2
