@@ -97,6 +97,8 @@ NCU_TRAFFIC = {
 def gemv_kernel_name(huffman: bool, tokens: int, x_bf16: bool = True) -> str:
     """The kernel cbq_linear_fixed / cbq_linear_huff dispatch to for `tokens` rows."""
     if huffman:
+        if tokens >= 64 and x_bf16:
+            return "k_huff_transcode + k_gemm_fixed"
         return "k_gemv_huff" if tokens == 1 else "k_linear_huff"
     if tokens <= 2:
         return "k_gemv_fixed"

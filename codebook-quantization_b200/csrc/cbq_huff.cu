@@ -24,6 +24,12 @@
 #include "cbq_hgemv_kernel.cuh"
 #include "cbq_huff_kernel.cuh"
 
+namespace cbq {
+int gemm_fixed(const void *x, int64_t T, int64_t ldx, const uint8_t *packed, const float *cb, int64_t C,
+               int bits, int64_t M, int64_t K, const float *bias, void *out, int out_dtype, int64_t ldo,
+               cudaStream_t s);
+}
+
 namespace {
 
 using namespace cbq;
@@ -265,6 +271,51 @@ __global__ void __launch_bounds__(256) k_huff_decode(const uint8_t *stream, uint
     if (bad) report(status, CBQ_FLAG_CORRUPT, (uint32_t)r);
 }
 
+// Huffman -> fixed-width transcode for the tensor-core prefill: thread g
+// decodes 64-symbol chunk q of row r (entered through the chunk table) and
+// writes its fields at BITS bits each, LSB-first: the chunk's 64 * BITS bits
+// are exactly the 2 * BITS words at word (r * K / 64 + q) * 2 * BITS of the
+// fixed-width stream (K % 64 == 0), so threads never share a word.  Symbols
+// are clamped to C - 1 as they are written (the reference's clamp), which
+// the GEMM would otherwise apply.
+template <int BITS>
+__global__ void __launch_bounds__(256) k_huff_transcode(const uint8_t *stream, uint64_t nwords,
+                                                        const HuffTables *tab, const int64_t *rbs,
+                                                        const uint32_t *chunk, int64_t M, int64_t K, int C,
+                                                        uint32_t *packed, uint32_t *status) {
+    __shared__ SmemTables st;
+    load_tables(&st, tab);
+    __syncthreads();
+    const int64_t nch = K / S;
+    const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (g >= M * nch) return;
+    const int64_t r = g / nch;
+    const uint16_t *gsyms = blob_syms(tab);
+    BitBuf bb;
+    bb.init(reinterpret_cast<const uint32_t *>(stream), nwords, (uint64_t)(rbs[r] + chunk[g]));
+    constexpr int NW = 2 * BITS;
+    constexpr uint32_t mask = (1u << BITS) - 1u;
+    uint32_t w[NW];
+#pragma unroll
+    for (int i = 0; i < NW; ++i) w[i] = 0u;
+    uint32_t bad = 0;
+#pragma unroll
+    for (int i = 0; i < S; ++i) {
+        int len;
+        // clamp (idx >= C -> C-1) here: the field then fits BITS = bits_for(C)
+        const uint32_t sym = min(decode_sym(bb.buf, &st, gsyms, len), (uint32_t)(C - 1)) & mask;
+        if (len == 0) { len = 1; ++bad; }
+        bb.consume(len);
+        const int bit = i * BITS, wi = bit >> 5, sh = bit & 31;
+        w[wi] |= sym << sh;
+        if (sh + BITS > 32) w[wi + 1] |= sym >> (32 - sh);
+    }
+    uint2 *dst = reinterpret_cast<uint2 *>(packed + g * NW);
+#pragma unroll
+    for (int i = 0; i < NW / 2; ++i) dst[i] = make_uint2(w[2 * i], w[2 * i + 1]);
+    if (bad) report(status, CBQ_FLAG_CORRUPT, (uint32_t)r);
+}
+
 template <typename OT>
 __global__ void __launch_bounds__(256) k_huff_embedding(const int64_t *ids, const uint8_t *stream,
                                                         uint64_t nwords,
@@ -391,10 +442,38 @@ int launch_hgemv(const HgArgs &a, const HgPlan &p, cudaStream_t s) {
     return CBQ_OK;
 }
 
-int64_t huff_workspace_bytes(int64_t M, int64_t K, int64_t T) {
+// Token count from which cbq_linear_huff transcodes to fixed width and runs
+// the tensor-core GEMM (bf16 activations).
+constexpr int64_t kHuffGemmMinTokens = 64;
+
+int64_t huff_split_bytes(int64_t M, int64_t K, int64_t T) {
     const int64_t nseg = ((K + S - 1) / S + 31) / 32;
     const int64_t TB = T >= 8 ? 8 : T >= 4 ? 4 : T >= 2 ? 2 : 1;
     return cbq_host::align_up(M * nseg * TB * 4, 256) + cbq_host::align_up(M * 4, 256);
+}
+
+// Fixed-width stream of the transcode at the widest supported width (16
+// bits), after the split-row workspace.
+int64_t huff_transcode_bytes(int64_t M, int64_t K) { return cbq_host::align_up(M * K * 2 + 64, 256); }
+
+int64_t huff_workspace_bytes(int64_t M, int64_t K, int64_t T) {
+    return huff_split_bytes(M, K, T) + (T >= kHuffGemmMinTokens ? huff_transcode_bytes(M, K) : 0);
+}
+
+int bits_for_entries(int64_t n) {
+    int b = 1;
+    while (b < 16 && (1ll << b) < n) ++b;
+    return b;
+}
+
+template <int BITS>
+int launch_transcode(const uint8_t *stream, int64_t stream_bytes, const HuffTables *tab, const int64_t *rbs,
+                     const uint32_t *chunk, int64_t M, int64_t K, int C, uint32_t *packed, uint32_t *status,
+                     cudaStream_t s) {
+    const int64_t n = M * (K / S);
+    k_huff_transcode<BITS><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(stream, (uint64_t)stream_bytes / 4, tab, rbs,
+                                                                      chunk, M, K, C, packed, status);
+    return cudaGetLastError() == cudaSuccess ? CBQ_OK : CBQ_ERR_CUDA;
 }
 
 template <int TB, typename XT>
@@ -574,6 +653,30 @@ extern "C" int cbq_linear_huff(const void *x_dev, int x_dtype, int64_t T, int64_
         h.out_bf16 = out_dtype == CBQ_BF16; h.cap = g.cap; h.status = status_dev;
         h.m4 = 4u; h.m16 = 1u << 16;
         return x_dtype == CBQ_BF16 ? launch_hgemv<__nv_bfloat16>(h, g, s) : launch_hgemv<float>(h, g, s);
+    }
+    // Many bf16 tokens: transcode the stream once to fixed width (in the
+    // workspace, after the split-row part) and run the tensor-core GEMM on
+    // it, so each symbol is entropy-decoded once per call instead of once per
+    // output tile.
+    if (T >= kHuffGemmMinTokens && x_dtype == CBQ_BF16 && workspace_dev &&
+        workspace_bytes >= huff_workspace_bytes(M, K, T) && K % (2 * S) == 0 && M % 128 == 0) {
+        const HuffTables *tab = static_cast<const HuffTables *>(tables_dev);
+        const int bits = bits_for_entries(std::max<int64_t>(C, 2));
+        if (bits <= 14) {
+            uint8_t *pk = static_cast<uint8_t *>(workspace_dev) + huff_split_bytes(M, K, T);
+            uint32_t *pw = reinterpret_cast<uint32_t *>(pk);
+            int rc = CBQ_ERR_ARG;
+            switch (bits) {
+#define CBQ_T(n) case n: rc = launch_transcode<n>(stream_dev, stream_bytes, tab, rbs_dev, chunk_dev, M, K, (int)C, \
+                                                   pw, status_dev, s); break;
+                CBQ_T(1) CBQ_T(2) CBQ_T(3) CBQ_T(4) CBQ_T(5) CBQ_T(6) CBQ_T(7)
+                CBQ_T(8) CBQ_T(9) CBQ_T(10) CBQ_T(11) CBQ_T(12) CBQ_T(13) CBQ_T(14)
+#undef CBQ_T
+            }
+            if (rc != CBQ_OK) return rc;
+            rc = gemm_fixed(x_dev, T, ldx, pk, codebook_dev, C, bits, M, K, bias_dev, out_dev, out_dtype, ldo, s);
+            if (rc != CBQ_ERR_UNSUPPORTED) return rc;
+        }
     }
     HuffPlan p;
     if (!plan_huff(M, K, T, total_bits, x_dtype == CBQ_BF16 ? 2 : 4, p)) return CBQ_ERR_UNSUPPORTED;

@@ -53,6 +53,13 @@ def read_status(status: torch.Tensor) -> Tuple[int, int, int]:
     return int(s[0]), int(s[1]), int(s[2])
 
 
+# Token count from which cbq_linear_huff transcodes the stream to fixed width
+# and runs the tensor-core GEMM (bf16 activations); the per-device scratch
+# that transcode lives in.
+PREFILL_TOKENS = 64
+_PREFILL_WS = {}
+
+
 class HuffmanStream:
     """Device-resident Huffman stream of one ``[rows, cols]`` tensor plus the
     derived decode tables and chunk-entry table."""
@@ -153,7 +160,17 @@ class HuffmanCodebookLinear:
         self._ws = {}
 
     def workspace(self, T: int) -> torch.Tensor:
-        """Zero-filled workspace for T-token calls (the kernels leave it zeroed)."""
+        """Zero-filled workspace for T-token calls (the kernels leave it zeroed).
+        From 64 tokens it also holds the fixed-width transcode the tensor-core
+        GEMM reads (2 bytes per weight at most); that buffer is one per device,
+        shared by every layer, so such calls on one device must share a stream."""
+        if T >= PREFILL_TOKENS:
+            n = _lib.query("cbq_linear_huff_workspace_bytes", self.M, self.K, int(T))
+            buf = _PREFILL_WS.get(self.device)
+            if buf is None or buf.numel() < n:
+                buf = torch.zeros(max(n, 16), dtype=torch.uint8, device=self.device)
+                _PREFILL_WS[self.device] = buf
+            return buf
         key = min(int(T), 8)
         ws = self._ws.get(key)
         if ws is None:

@@ -369,7 +369,13 @@ int cbq_huff_build_decode_lut(const void *tables_dev, const float *codebook_dev,
                               uint32_t *lut_dev, void *stream);
 
 /* Workspace bytes cbq_linear_huff may use (same contract as
- * cbq_linear_fixed_workspace_bytes). */
+ * cbq_linear_fixed_workspace_bytes).  From 64 tokens this includes room for
+ * the stream transcoded to fixed width (2 * M * K bytes at most): with it,
+ * bf16 activations, M % 128 == 0, K % 128 == 0 and C <= 16384, the call
+ * first rewrites the Huffman stream as a b-bit LSB-first stream (b =
+ * ceil(log2 C), indices clamped to C - 1) in the workspace and then runs the
+ * tensor-core GEMM of cbq_linear_fixed on it, so every symbol is
+ * entropy-decoded once per call; without it the CUDA-core kernel runs. */
 int64_t cbq_linear_huff_workspace_bytes(int64_t M, int64_t K, int64_t T);
 
 /* Fused Huffman decode + GEMV: same result as cbq_linear_fixed on the

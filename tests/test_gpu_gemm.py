@@ -56,3 +56,26 @@ def test_gemm_is_deterministic():
     lin, _, _ = _lin(dev, 256, 512, 13, seed=9)
     x = torch.randn(200, 512, device=dev).to(torch.bfloat16)
     assert torch.equal(lin(x), lin(x))
+
+
+@pytest.mark.parametrize("M,K,T,bits", [(128, 128, 64, 13), (256, 512, 300, 12), (384, 1024, 256, 8),
+                                        (128, 4096, 96, 14), (256, 256, 70, 5)])
+def test_huffman_prefill_transcode_gemm_matches_oracle(M, K, T, bits):
+    """Huffman streams with 64 or more bf16 tokens: transcoded once to fixed
+    width in the workspace, then the tensor-core GEMM (rel-L2 1e-5 with a
+    bf16-exact codebook; indices at or above C clamp)."""
+    dev = need_cuda()
+    rng = np.random.default_rng(M + K + T)
+    C = (1 << bits) - 3
+    cb = ((rng.standard_normal(C) * 0.02).astype(np.float32).view(np.uint32) & 0xFFFF0000).view(np.float32)
+    idx = np.minimum(rng.zipf(1.3, size=(M, K)) - 1, (1 << bits) - 1).astype(np.uint16)   # skewed, some >= C
+    d = cbq.huffman_codebook.huffman_encode_indices(idx.reshape(-1), shape=(M, K))
+    lin = cbq.HuffmanCodebookLinear("h", d["huff_stream"], d["huff_lengths"], int(d["huff_n"][0]), cb, (M, K), bits,
+                                    huff_row_bit_starts=d["huff_row_bit_starts"], device=dev)
+    x = torch.randn(T, K, device=dev).to(torch.bfloat16)
+    y = lin(x, out_dtype=torch.float32).cpu().numpy()
+    lin.hs.check()
+    ref = oracle.huff_linear(x.float().cpu().numpy(), d, cb, M, K)
+    assert rel_l2(y, ref) < 1e-5
+    y16 = lin(x).float().cpu().numpy()
+    assert rel_l2(y16, ref) < 1e-2
