@@ -19,6 +19,10 @@ namespace cbq {
 int gemm_fixed(const void *x, int64_t T, int64_t ldx, const uint8_t *packed, const float *cb, int64_t C,
                int bits, int64_t M, int64_t K, const float *bias, void *out, int out_dtype, int64_t ldo,
                cudaStream_t s);
+int gemm_small(const void *x, int64_t T, int64_t ldx, const uint8_t *packed, const float *cb, int64_t C, int bits,
+               int64_t M, int64_t K, const float *bias, void *out, int out_dtype, int64_t ldo, void *ws,
+               int64_t ws_bytes, cudaStream_t s);
+int64_t gemm_small_workspace_bytes(int64_t M, int64_t K, int64_t T);
 template <int BITS>
 int launch_fixed_bits(int TB, bool x_bf16, const FixedArgs &a, size_t smem, int grid, cudaStream_t s);
 template <int BITS>
@@ -143,10 +147,16 @@ bool plan_fixed(int64_t M, int64_t K, int bits, int64_t C, int64_t T, int xbytes
     return true;
 }
 
+// Token counts served by the small-batch tensor-core GEMM (bf16 activations).
+constexpr int64_t kSmallGemmMinTokens = 3;
+
 int64_t workspace_bytes_for(int64_t M, int64_t K, int64_t T) {
     const int64_t nseg = (K + kFxSeg - 1) / kFxSeg;
     const int64_t TB = T >= 8 ? 8 : T >= 4 ? 4 : T >= 2 ? 2 : 1;
-    return cbq_host::align_up(M * nseg * TB * 4, 256) + cbq_host::align_up(M * 4, 256);
+    const int64_t split_rows = cbq_host::align_up(M * nseg * TB * 4, 256) + cbq_host::align_up(M * 4, 256);
+    // 3..63 tokens: also the split-K partial tiles of the tensor-core path
+    const int64_t small = (T >= kSmallGemmMinTokens && T < 64) ? gemm_small_workspace_bytes(M, K, T) : 0;
+    return std::max(split_rows, small);
 }
 
 // Token count from which cbq_linear_fixed uses the tensor-core GEMM.
@@ -237,6 +247,15 @@ int linear_fixed_impl(const void *x, int x_dtype, int64_t T, int64_t ldx, const 
     if (T >= kGemmMinTokens && x_dtype == CBQ_BF16) {
         const int rc = gemm_fixed(x, T, ldx, packed, cb, C, bits, M, K, bias, out, out_dtype, ldo, s);
         if (rc != CBQ_ERR_UNSUPPORTED) return rc;
+    }
+    // 3..63 bf16 tokens (decode batches): the split-K tensor-core GEMM
+    if (T >= kSmallGemmMinTokens && T < kGemmMinTokens && x_dtype == CBQ_BF16) {
+        const int64_t need = gemm_small_workspace_bytes(M, K, T);
+        if (need == 0 || (ws && ws_bytes >= need)) {
+            if (need > 0 && ws_mode == kWsClearFirst) CBQ_CUDA_TRY(cudaMemsetAsync(ws, 0, (size_t)need, s));
+            const int rc = gemm_small(x, T, ldx, packed, cb, C, bits, M, K, bias, out, out_dtype, ldo, ws, ws_bytes, s);
+            if (rc != CBQ_ERR_UNSUPPORTED) return rc;
+        }
     }
     GemvPlan g;
     if (aligned && x_aligned && plan_gemv(M, K, bits, C, T, g)) {

@@ -36,13 +36,21 @@ namespace {
 using namespace cbq;
 
 constexpr int kBM = 128, kBN = 256, kBK = 64;
-constexpr int kPStages = 2;                           // packed-index tiles (two K steps each) in flight
-// operand stages (A + B): as many as shared memory allows next to the
-// packed tiles and the bf16 codebook
-template <int BITS> struct GemmCfg {
-    static constexpr int kStages = BITS <= 13 ? 3 : 2;
+// Two shapes of one kernel:
+//   BN = 256 (prefill): output tiles of 128 rows x 256 tokens, 3 operand
+//     stages (2 for b = 14), 2 packed tiles in flight;
+//   BN = 16 / 32 / 64 (3..63 tokens, decode batches): one token tile, the
+//     K range split over several CTAs (split-K) so every SM decodes, 4
+//     operand stages and 4 packed tiles in flight (the decode and the index
+//     stream, not the tensor core, bound these shapes).
+template <int BITS, int BN> struct GemmCfg {
+    static constexpr bool kSmall = BN < 256;
+    static constexpr int kStages = kSmall ? 4 : (BITS <= 13 ? 3 : 2);
+    static constexpr int kPStages = kSmall ? 4 : 2;              // packed-index tiles (two K steps each)
     static constexpr uint32_t kPRowBytes = 16u * BITS;           // 128 indices of one row
     static constexpr uint32_t kPBytes = kBM * kPRowBytes;         // one packed tile
+    static constexpr uint32_t kBBytes = BN * kBK * 2;             // one x tile
+    static constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;      // allocation granularity is 32 columns
 };
 constexpr int kSetThreads = 256;                      // a decoder set: two threads per tile row
 constexpr int kSets = 2;                              // sets decode alternate K steps
@@ -50,8 +58,6 @@ constexpr int kDecoders = kSets * kSetThreads;
 constexpr int kDecWarps = kDecoders / 32;
 constexpr int kThreads = kDecoders + 64;              // + TMA warp + MMA warp
 constexpr uint32_t kABytes = kBM * kBK * 2;           // 16 KB
-constexpr uint32_t kBBytes = kBN * kBK * 2;           // 32 KB
-constexpr uint32_t kTmemCols = 256;
 
 struct GemmArgs {
     const uint8_t *packed;
@@ -65,6 +71,14 @@ struct GemmArgs {
     int tiles_m, tiles_n;
     uint32_t cb_entries;              // bf16 codebook entries in shared memory (padded to 2^b)
     uint32_t *status;
+    // split-K (BN < 256): the K steps of an output tile are split over
+    // `splits` work items; each writes its partial tile (fp32) to part
+    // [splits][tiles_n * BN][M] and counts its arrival per (tile, epilogue
+    // warp) on cnt; the item that completes a warp's count adds the partials
+    // in split order and writes y, then resets the count (left 0).
+    int splits;
+    float *part;
+    uint32_t *cnt;
 };
 
 // ---------------------------------------------------------------- PTX helpers
@@ -100,6 +114,38 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
         ::"r"(smem_u32(dst)), "l"(map), "r"(c0), "r"(c1), "r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]);
+
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
+                 "[%16];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                   "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+                 : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Width-W (4 <= W <= 32, power of two) read of this warp's 32 TMEM lanes.
+template <int W>
+__device__ __forceinline__ void tmem_ldw(uint32_t taddr, uint32_t (&v)[W]) {
+    if constexpr (W == 32) tmem_ld32(taddr, v);
+    else if constexpr (W == 16) tmem_ld16(taddr, v);
+    else if constexpr (W == 8) tmem_ld8(taddr, v);
+    else {
+        uint32_t t[8];
+        tmem_ld8(taddr, t);
+#pragma unroll
+        for (int j = 0; j < W; ++j) v[j] = t[j];
+    }
 }
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
@@ -167,12 +213,32 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, vo
     return false;
 }
 
-template <int BITS>
+// Work item `tile` -> output tile (tm, tn), split sp and its K steps
+// [kb, ke) (whole packed tiles: kb, ke even).
+struct GemmItem {
+    int tm, tn, sp, kb, ke;
+};
+__device__ __forceinline__ GemmItem gemm_item(const GemmArgs &a, int tile, int nk) {
+    GemmItem it;
+    const int per_m = a.tiles_n * a.splits;
+    it.tm = tile / per_m;
+    const int rem = tile - it.tm * per_m;
+    it.tn = rem / a.splits;
+    it.sp = rem - it.tn * a.splits;
+    const int npair = nk / 2, ppw = (npair + a.splits - 1) / a.splits;
+    it.kb = 2 * min(it.sp * ppw, npair);
+    it.ke = 2 * min(it.sp * ppw + ppw, npair);
+    return it;
+}
+
+template <int BITS, int BN>
 __global__ void __launch_bounds__(kThreads, 1) k_gemm_fixed(const __grid_constant__ CUtensorMap tmap_x,
                                                             const __grid_constant__ CUtensorMap tmap_p,
                                                             const GemmArgs a) {
-    constexpr int kStages = GemmCfg<BITS>::kStages;
-    constexpr uint32_t kPRowBytes = GemmCfg<BITS>::kPRowBytes, kPBytes = GemmCfg<BITS>::kPBytes;
+    using Cfg = GemmCfg<BITS, BN>;
+    constexpr int kStages = Cfg::kStages, kPStages = Cfg::kPStages;
+    constexpr uint32_t kPRowBytes = Cfg::kPRowBytes, kPBytes = Cfg::kPBytes, kBBytes = Cfg::kBBytes;
+    constexpr uint32_t kTmemCols = Cfg::kTmemCols;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte aligned base for the swizzled operand tiles
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -218,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_fixed(const __grid_constan
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const int nk = a.K / kBK;
-    const int ntiles = a.tiles_m * a.tiles_n;
+    const int ntiles = a.tiles_m * a.tiles_n * a.splits;
 
     if (warp < kDecWarps) {
         // ------------------------------------------------ decoders + epilogue
@@ -233,12 +299,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_fixed(const __grid_constan
         uint32_t acc_phase = 0;
         bool go = true;
         pdl_wait();                                           // x and y belong to the stream's previous work
-        for (int tile = blockIdx.x; tile < ntiles && go; tile += gridDim.x, base_it += nk) {
-            const int tm = tile / a.tiles_n, tn = tile - tm * a.tiles_n;
+        for (int tile = blockIdx.x; tile < ntiles && go; tile += gridDim.x) {
+            const GemmItem wi = gemm_item(a, tile, nk);
+            const int tm = wi.tm, tn = wi.tn;
             uint32_t w[NW + 1];
-            for (int k = g; k < nk; k += kSets) {
+            for (int k = wi.kb + g; k < wi.ke; k += kSets) {
                 // this row's words of step k from the packed tile (two steps per tile)
-                const int pi = (base_it + k) >> 1;            // packed tiles used before
+                const int pi = (base_it + k - wi.kb) >> 1;    // packed tiles used before
                 const int ps = pi % kPStages;
                 if (!wait_or_abort(&full_p[ps], (pi / kPStages) & 1, abort_flag, a)) {
                     go = false;
@@ -257,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_fixed(const __grid_constan
                 }
                 w[NW] = 0u;
                 mbar_arrive(&empty_p[ps]);                    // words are in registers
-                const int it = base_it + k;
+                const int it = base_it + k - wi.kb;
                 const int s = it % kStages;
                 if (it >= kStages && !wait_or_abort(&empty[s], ((it / kStages) - 1) & 1, abort_flag, a)) {
                     go = false;
@@ -279,32 +346,71 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_fixed(const __grid_constan
                 fence_proxy_async_smem();                     // generic stores -> tensor-core reads
                 mbar_arrive(&full_a[s]);
             }
+            base_it += wi.ke - wi.kb;
             if (!go) break;
             // epilogue: TMEM lanes 32*(warp%4).. = tile rows; the four warps of
-            // a lane quarter take 64 accumulator columns each
+            // a lane quarter take BN/4 accumulator columns each
             if (!wait_or_abort(acc_full, acc_phase, abort_flag, a)) { go = false; break; }
             acc_phase ^= 1u;
             tc_fence_after();
             const int er = (warp & 3) * 32 + lane;
             const int64_t m = (int64_t)tm * kBM + er;
             const float b = a.bias ? a.bias[m] : 0.f;
-            const int cbeg = (warp >> 2) * (kBN / 4);
+            constexpr int kWc = BN / 4;                        // columns per warp
+            constexpr int kCW = kWc < 32 ? kWc : 32;           // columns per TMEM load
+            const int cbeg = (warp >> 2) * kWc;
+            auto store_y = [&](int64_t tt, float y) {
+                if (a.out_bf16) static_cast<__nv_bfloat16 *>(a.out)[tt * a.ldo + m] = __float2bfloat16_rn(y);
+                else static_cast<float *>(a.out)[tt * a.ldo + m] = y;
+            };
+            if (a.splits == 1) {
 #pragma unroll 1
-            for (int c0 = cbeg; c0 < cbeg + kBN / 4; c0 += 32) {
-                uint32_t v[32];
-                tmem_ld32(tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)c0, v);
+                for (int c0 = cbeg; c0 < cbeg + kWc; c0 += kCW) {
+                    uint32_t v[kCW];
+                    tmem_ldw<kCW>(tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)c0, v);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int64_t tt = (int64_t)tn * kBN + c0 + j;
-                    if (tt < a.T) {
-                        const float y = __uint_as_float(v[j]) + b;
-                        if (a.out_bf16) static_cast<__nv_bfloat16 *>(a.out)[tt * a.ldo + m] = __float2bfloat16_rn(y);
-                        else static_cast<float *>(a.out)[tt * a.ldo + m] = y;
+                    for (int j = 0; j < kCW; ++j) {
+                        const int64_t tt = (int64_t)tn * BN + c0 + j;
+                        if (tt < a.T) store_y(tt, __uint_as_float(v[j]) + b);
                     }
                 }
+                tc_fence_before();
+                mbar_arrive(acc_empty);
+            } else {
+                // split-K: this warp's 32 rows x kWc columns as a partial tile
+                const int64_t tpad = (int64_t)a.tiles_n * BN;
+                uint32_t v[kWc];
+#pragma unroll
+                for (int c0 = 0; c0 < kWc; c0 += kCW) {
+                    uint32_t t[kCW];
+                    tmem_ldw<kCW>(tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(cbeg + c0), t);
+#pragma unroll
+                    for (int j = 0; j < kCW; ++j) v[c0 + j] = t[j];
+                }
+                tc_fence_before();
+                mbar_arrive(acc_empty);                       // the accumulator is in registers
+#pragma unroll
+                for (int j = 0; j < kWc; ++j)
+                    a.part[((int64_t)wi.sp * tpad + (int64_t)tn * BN + cbeg + j) * a.M + m] = __uint_as_float(v[j]);
+                __threadfence();
+                __syncwarp();
+                uint32_t old = 0;
+                uint32_t *cw = a.cnt + ((int64_t)tm * a.tiles_n + tn) * kDecWarps + warp;
+                if (lane == 0) old = atomicAdd(cw, 1u);
+                old = __shfl_sync(0xffffffffu, old, 0);
+                if (old == (uint32_t)(a.splits - 1)) {          // this warp's partition is complete
+                    __threadfence();
+#pragma unroll 1
+                    for (int j = 0; j < kWc; ++j) {
+                        const int64_t tt = (int64_t)tn * BN + cbeg + j;
+                        float y = 0.f;
+                        for (int sp = 0; sp < a.splits; ++sp)
+                            y += __ldcg(a.part + ((int64_t)sp * tpad + tt) * a.M + m);
+                        if (tt < a.T) store_y(tt, y + b);
+                    }
+                    if (lane == 0) *cw = 0u;
+                }
             }
-            tc_fence_before();
-            mbar_arrive(acc_empty);
         }
     } else if (warp == kDecWarps) {
         // ------------------------------------------------------------ TMA (x)
@@ -313,9 +419,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_fixed(const __grid_constan
             bool go = true;
             pdl_wait();
             for (int tile = blockIdx.x; tile < ntiles && go; tile += gridDim.x) {
-                const int tm = tile / a.tiles_n, tn = tile - tm * a.tiles_n;
-                for (int k = 0; k < nk; ++k, ++it) {
-                    if ((k & 1) == 0) {                       // packed tile of steps k, k+1
+                const GemmItem wi = gemm_item(a, tile, nk);
+                const int tm = wi.tm, tn = wi.tn;
+                for (int k = wi.kb; k < wi.ke; ++k, ++it) {
+                    if (((k - wi.kb) & 1) == 0) {             // packed tile of steps k, k+1
                         const int pi = it >> 1, ps = pi % kPStages;
                         if (pi >= kPStages &&
                             !wait_or_abort(&empty_p[ps], ((pi / kPStages) - 1) & 1, abort_flag, a)) {
@@ -332,7 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_fixed(const __grid_constan
                         break;
                     }
                     mbar_arrive_expect_tx(&full_b[s], kBBytes);
-                    tma_load_2d(sB + (size_t)s * kBBytes, &tmap_x, k * kBK, tn * kBN, &full_b[s]);
+                    tma_load_2d(sB + (size_t)s * kBBytes, &tmap_x, k * kBK, tn * BN, &full_b[s]);
                 }
             }
             // No load may still be landing when the CTA exits: wait (bounded)
@@ -350,13 +457,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_fixed(const __grid_constan
     } else {
         // ------------------------------------------------------------- MMA issue
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_bf16(kBM, kBN);
+            constexpr uint32_t idesc = idesc_bf16(kBM, BN);
             int it = 0, nt = 0;
             bool go = true;
             for (int tile = blockIdx.x; tile < ntiles && go; tile += gridDim.x, ++nt) {
+                const GemmItem wi = gemm_item(a, tile, nk);
                 if (nt > 0 && !wait_or_abort(acc_empty, (nt - 1) & 1, abort_flag, a)) { go = false; break; }
                 tc_fence_after();
-                for (int k = 0; k < nk; ++k, ++it) {
+                for (int k = wi.kb; k < wi.ke; ++k, ++it) {
                     const int s = it % kStages;
                     const uint32_t ph = (it / kStages) & 1;
                     if (!wait_or_abort(&full_a[s], ph, abort_flag, a) ||
@@ -369,7 +477,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_fixed(const __grid_constan
 #pragma unroll
                     for (int kk = 0; kk < kBK / 16; ++kk)
                         mma_bf16(tmem, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32), idesc,
-                                 (k > 0 || kk > 0) ? 1u : 0u);
+                                 (k > wi.kb || kk > 0) ? 1u : 0u);
                     mma_commit(&empty[s]);                    // frees the stage when these MMAs finish
                 }
                 if (!go) break;
@@ -408,18 +516,19 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-template <int BITS>
+template <int BITS, int BN>
 size_t gemm_smem_bytes(uint32_t cb_entries) {
-    return 1024 + (size_t)GemmCfg<BITS>::kStages * (kABytes + kBBytes) + kPStages * a128(GemmCfg<BITS>::kPBytes) +
+    using Cfg = GemmCfg<BITS, BN>;
+    return 1024 + (size_t)Cfg::kStages * (kABytes + Cfg::kBBytes) + Cfg::kPStages * a128(Cfg::kPBytes) +
            a128((size_t)cb_entries * 2) + 256;
 }
 
-template <int BITS>
+template <int BITS, int BN>
 int launch_gemm(const CUtensorMap &map, const CUtensorMap &pmap, GemmArgs a, cudaStream_t s) {
-    const size_t smem = gemm_smem_bytes<BITS>(a.cb_entries);
+    const size_t smem = gemm_smem_bytes<BITS, BN>(a.cb_entries);
     if (smem > (size_t)cbq_host::max_smem_optin()) return CBQ_ERR_UNSUPPORTED;
-    const int grid = (int)std::min<int64_t>((int64_t)a.tiles_m * a.tiles_n, cbq_host::sm_count());
-    auto kern = k_gemm_fixed<BITS>;
+    const int grid = (int)std::min<int64_t>((int64_t)a.tiles_m * a.tiles_n * a.splits, cbq_host::sm_count());
+    auto kern = k_gemm_fixed<BITS, BN>;
     static std::mutex mu;
     static size_t configured[64] = {0};
     int dev = 0;
@@ -435,9 +544,105 @@ int launch_gemm(const CUtensorMap &map, const CUtensorMap &pmap, GemmArgs a, cud
     return CBQ_OK;
 }
 
+// Split count for the small-batch shape: the number of work items
+// (row tiles x splits) that fills the SMs in the fewest waves per unit of
+// work, at most one split per pair of K steps and at most 32.
+int choose_splits(int64_t tiles, int64_t npair) {
+    const int64_t sms = cbq_host::sm_count();
+    int best = 1;
+    double best_cost = 1e30;
+    for (int sp = 1; sp <= 32 && sp <= npair; ++sp) {
+        const int64_t ppw = (npair + sp - 1) / sp;
+        if ((int64_t)(sp - 1) * ppw >= npair) continue;           // an empty split
+        const double waves = (double)((tiles * sp + sms - 1) / sms);
+        const double cost = waves * (double)ppw + 0.02 * sp * npair / sp;   // + the partial tiles' traffic
+        if (cost < best_cost - 1e-9) {
+            best_cost = cost;
+            best = sp;
+        }
+    }
+    return best;
+}
+
+// Tensor maps of the activations (bf16 [T, K], box BN x 64) and of the packed
+// stream as a [M rows, K*bits/8 bytes] byte matrix (box 128 rows x 16*bits
+// bytes = two K steps, a 16-byte multiple for every width).
+bool gemm_maps(const void *x, int64_t T, int64_t ldx, const uint8_t *packed, int bits, int64_t M, int64_t K, int BN,
+               CUtensorMap &map, CUtensorMap &pmap) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)T};
+    const cuuint64_t strides[1] = {(cuuint64_t)ldx * 2};
+    const cuuint32_t box[2] = {kBK, (cuuint32_t)BN};
+    const cuuint32_t estr[2] = {1, 1};
+    if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(x), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    const cuuint64_t row_bytes = (cuuint64_t)K * bits / 8;
+    const cuuint64_t pdims[2] = {row_bytes, (cuuint64_t)M};
+    const cuuint64_t pstrides[1] = {row_bytes};
+    const cuuint32_t pbox[2] = {(cuuint32_t)(16 * bits), (cuuint32_t)kBM};
+    return enc(&pmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(packed), pdims, pstrides, pbox, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN>
+int launch_gemm_bits(int bits, const CUtensorMap &map, const CUtensorMap &pmap, const GemmArgs &a, cudaStream_t s) {
+    switch (bits) {
+#define CBQ_G(n) case n: return launch_gemm<n, BN>(map, pmap, a, s);
+        CBQ_G(1) CBQ_G(2) CBQ_G(3) CBQ_G(4) CBQ_G(5) CBQ_G(6) CBQ_G(7)
+        CBQ_G(8) CBQ_G(9) CBQ_G(10) CBQ_G(11) CBQ_G(12) CBQ_G(13) CBQ_G(14)
+#undef CBQ_G
+    }
+    return CBQ_ERR_UNSUPPORTED;
+}
+
 }  // namespace
 
 namespace cbq {
+
+int64_t gemm_small_workspace_bytes(int64_t M, int64_t K, int64_t T) {
+    if (T < 1 || T > 64 || M % kBM || K % (2 * kBK)) return 0;
+    const int BN = T <= 32 ? 32 : 64;
+    const int sp = choose_splits(M / kBM, K / (2 * kBK));
+    if (sp == 1) return 0;
+    return cbq_host::align_up((int64_t)sp * BN * M * 4, 256) + cbq_host::align_up((M / kBM) * kDecWarps * 4, 256);
+}
+
+// Small-batch decode-GEMM (3..64 bf16 tokens) on the tensor cores with
+// split-K: one 32- or 64-token tile, each 128-row tile's K range split over
+// several CTAs (their partial tiles in the workspace, combined in split
+// order by the last one), so all SMs decode.  CBQ_ERR_UNSUPPORTED (nothing
+// launched) outside its shapes or when the workspace is too small.
+int gemm_small(const void *x, int64_t T, int64_t ldx, const uint8_t *packed, const float *cb, int64_t C, int bits,
+               int64_t M, int64_t K, const float *bias, void *out, int out_dtype, int64_t ldo, void *ws,
+               int64_t ws_bytes, cudaStream_t s) {
+    if (bits < 1 || bits > 14 || M % kBM || K % (2 * kBK) || K <= 0 || T < 1 || T > 64 || M <= 0)
+        return CBQ_ERR_UNSUPPORTED;
+    if ((reinterpret_cast<uintptr_t>(x) & 15) || (ldx * 2) % 16 || (reinterpret_cast<uintptr_t>(packed) & 15))
+        return CBQ_ERR_UNSUPPORTED;
+    if (M >= (1ll << 31) || K >= (1ll << 31)) return CBQ_ERR_UNSUPPORTED;
+    const int BN = T <= 32 ? 32 : 64;
+    const int sp = choose_splits(M / kBM, K / (2 * kBK));
+    const int64_t need = gemm_small_workspace_bytes(M, K, T);
+    if (sp > 1 && (!ws || ws_bytes < need)) return CBQ_ERR_UNSUPPORTED;
+    CUtensorMap map, pmap;
+    if (!gemm_maps(x, T, ldx, packed, bits, M, K, BN, map, pmap)) return CBQ_ERR_UNSUPPORTED;
+    GemmArgs a{};
+    a.packed = packed; a.codebook = cb; a.C = (int)C; a.bits = bits;
+    a.M = (int)M; a.K = (int)K; a.T = (int)T; a.bias = bias; a.out = out; a.ldo = ldo;
+    a.out_bf16 = out_dtype == CBQ_BF16; a.tiles_m = (int)(M / kBM); a.tiles_n = 1;
+    a.cb_entries = std::max<uint32_t>((uint32_t)C, 1u << bits); a.status = nullptr;
+    a.splits = sp;
+    if (sp > 1) {
+        a.part = static_cast<float *>(ws);
+        a.cnt = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(ws) +
+                                             cbq_host::align_up((int64_t)sp * BN * M * 4, 256));
+    }
+    return BN == 32 ? launch_gemm_bits<32>(bits, map, pmap, a, s) : launch_gemm_bits<64>(bits, map, pmap, a, s);
+}
 
 // Prefill GEMM entry used by cbq_linear_fixed for many tokens.  Returns
 // CBQ_ERR_UNSUPPORTED (nothing launched) outside its shapes: bf16 x with
@@ -476,14 +681,8 @@ int gemm_fixed(const void *x, int64_t T, int64_t ldx, const uint8_t *packed, con
     a.packed = packed; a.codebook = cb; a.C = (int)C; a.bits = bits;
     a.M = (int)M; a.K = (int)K; a.T = (int)T; a.bias = bias; a.out = out; a.ldo = ldo;
     a.out_bf16 = out_dtype == CBQ_BF16; a.tiles_m = (int)(M / kBM); a.tiles_n = (int)((T + kBN - 1) / kBN);
-    a.cb_entries = entries; a.status = nullptr;
-    switch (bits) {
-#define CBQ_G(n) case n: return launch_gemm<n>(map, pmap, a, s);
-        CBQ_G(1) CBQ_G(2) CBQ_G(3) CBQ_G(4) CBQ_G(5) CBQ_G(6) CBQ_G(7)
-        CBQ_G(8) CBQ_G(9) CBQ_G(10) CBQ_G(11) CBQ_G(12) CBQ_G(13) CBQ_G(14)
-#undef CBQ_G
-    }
-    return CBQ_ERR_UNSUPPORTED;
+    a.cb_entries = entries; a.status = nullptr; a.splits = 1;
+    return launch_gemm_bits<kBN>(bits, map, pmap, a, s);
 }
 
 }  // namespace cbq

@@ -119,8 +119,9 @@ class GPUAcceleratedLinear:
         self._ws = {}                      # token-block size -> zero-filled workspace
 
     def workspace(self, T: int) -> torch.Tensor:
-        """Zero-filled workspace for T-token calls (the kernels leave it zeroed)."""
-        key = min(int(T), 8)
+        """Zero-filled workspace for T-token calls (the kernels leave it zeroed);
+        3..63 tokens size it for the split-K tensor-core path too."""
+        key = int(T) if 3 <= int(T) < 64 else min(int(T), 8)
         ws = self._ws.get(key)
         if ws is None:
             n = _lib.query("cbq_linear_fixed_workspace_bytes", self.M, self.K, key)

@@ -79,3 +79,24 @@ def test_huffman_prefill_transcode_gemm_matches_oracle(M, K, T, bits):
     assert rel_l2(y, ref) < 1e-5
     y16 = lin(x).float().cpu().numpy()
     assert rel_l2(y16, ref) < 1e-2
+
+
+@pytest.mark.parametrize("M,K,T,bits", [(128, 256, 3, 13), (1024, 4096, 8, 13), (384, 1024, 5, 8), (12288, 4096, 8, 13),
+                                        (4096, 12288, 8, 13), (256, 512, 33, 12), (640, 2048, 63, 14),
+                                        (2048, 2048, 16, 4)])
+def test_small_batch_tensor_core_gemm_matches_oracle(M, K, T, bits):
+    """3..63 bf16 tokens (decode batches): the split-K tensor-core GEMM (one
+    32/64-token tile, each row tile's K range over several CTAs, partial tiles
+    combined in split order by the last one), two calls in a row (the arrival
+    counters are reused): rel-L2 1e-5 against the oracle with a bf16-exact
+    codebook, bit-identical between the calls."""
+    dev = need_cuda()
+    lin, packed, cb = _lin(dev, M, K, bits, seed=M + K + T)
+    outs = []
+    for _ in range(2):
+        x = torch.randn(T, K, device=dev, generator=torch.Generator(device=dev).manual_seed(T)).to(torch.bfloat16)
+        y = lin(x, out_dtype=torch.float32)
+        outs.append(y)
+    ref = oracle.linear_fixed(x.float().cpu().numpy(), packed, cb, M, K, bits)
+    assert rel_l2(outs[1].cpu().numpy(), ref) < 1e-5
+    assert torch.equal(outs[0], outs[1])
