@@ -58,6 +58,7 @@ constexpr int kDecoders = kSets * kSetThreads;
 constexpr int kDecWarps = kDecoders / 32;
 constexpr int kThreads = kDecoders + 64;              // + TMA warp + MMA warp
 constexpr uint32_t kABytes = kBM * kBK * 2;           // 16 KB
+constexpr int kMaxSplits = 4;                          // split-K: K ranges per output tile at most
 
 struct GemmArgs {
     const uint8_t *packed;
@@ -400,12 +401,23 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_fixed(const __grid_constan
                 old = __shfl_sync(0xffffffffu, old, 0);
                 if (old == (uint32_t)(a.splits - 1)) {          // this warp's partition is complete
                     __threadfence();
-#pragma unroll 1
+                    // every split's values of the partition, all loads issued
+                    // first, then added in split order
+                    float pv[kMaxSplits][kWc];
+#pragma unroll
+                    for (int sp = 0; sp < kMaxSplits; ++sp)
+#pragma unroll
+                        for (int j = 0; j < kWc; ++j)
+                            pv[sp][j] = sp < a.splits
+                                            ? __ldcg(a.part + ((int64_t)sp * tpad + (int64_t)tn * BN + cbeg + j) * a.M + m)
+                                            : 0.f;
+#pragma unroll
                     for (int j = 0; j < kWc; ++j) {
                         const int64_t tt = (int64_t)tn * BN + cbeg + j;
                         float y = 0.f;
-                        for (int sp = 0; sp < a.splits; ++sp)
-                            y += __ldcg(a.part + ((int64_t)sp * tpad + tt) * a.M + m);
+#pragma unroll
+                        for (int sp = 0; sp < kMaxSplits; ++sp)
+                            if (sp < a.splits) y += pv[sp][j];
                         if (tt < a.T) store_y(tt, y + b);
                     }
                     if (lane == 0) *cw = 0u;
@@ -546,16 +558,18 @@ int launch_gemm(const CUtensorMap &map, const CUtensorMap &pmap, GemmArgs a, cud
 
 // Split count for the small-batch shape: the number of work items
 // (row tiles x splits) that fills the SMs in the fewest waves per unit of
-// work, at most one split per pair of K steps and at most 32.
+// work, at most one split per pair of K steps and at most kMaxSplits.
 int choose_splits(int64_t tiles, int64_t npair) {
+    // time ~ waves x (pairs of K steps per item + a fixed per-item cost of
+    // about two pairs: pipeline refill and the partial-tile epilogue)
     const int64_t sms = cbq_host::sm_count();
     int best = 1;
     double best_cost = 1e30;
-    for (int sp = 1; sp <= 32 && sp <= npair; ++sp) {
+    for (int sp = 1; sp <= kMaxSplits && sp <= npair; ++sp) {
         const int64_t ppw = (npair + sp - 1) / sp;
         if ((int64_t)(sp - 1) * ppw >= npair) continue;           // an empty split
         const double waves = (double)((tiles * sp + sms - 1) / sms);
-        const double cost = waves * (double)ppw + 0.02 * sp * npair / sp;   // + the partial tiles' traffic
+        const double cost = waves * ((double)ppw + 2.0);
         if (cost < best_cost - 1e-9) {
             best_cost = cost;
             best = sp;
