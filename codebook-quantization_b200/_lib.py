@@ -77,6 +77,7 @@ SIGNATURES = {
     "cbq_rmsnorm": (_INT, [_P, _P, _INT, _I64, _I64, _P, ct.c_float, _P, _P]),
     "cbq_rmsnorm_allreduce": (_INT, [_P, _P, _P, _P, _I64, _INT, _INT, _I64, _I64, _P, ct.c_float, _P, _P,
                                      _P]),
+    "cbq_greedy_pick": (_INT, [_P, _INT, _I64, _I64, _I64, _INT, _INT, _P, _P, _P, _P, _P, _P]),
     "cbq_qk_norm_rope": (_INT, [_P, _P, _P, _INT, _I64, _I64, _I64, _I64, ct.c_float, _P, _P, _P, _P, _P,
                                 _P, _P, _P, _I64, _P]),
     "cbq_attn_decode": (_INT, [_P, _P, _P, _INT, _I64, _I64, _I64, _I64, _I64, _P, ct.c_float, _P, _P]),

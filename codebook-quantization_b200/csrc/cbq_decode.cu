@@ -9,6 +9,7 @@
 // the same points as the unfused torch sequence; reductions (sum of squares,
 // softmax, the attention-weighted sum) accumulate in fp32.
 #include <algorithm>
+#include <climits>
 
 #include "cbq_common.cuh"
 
@@ -467,9 +468,126 @@ __global__ void __launch_bounds__(D) k_attn_decode(const T *q, T *k_cache, T *v_
     if (threadIdx.x == 0) sp.count[bg] = 0u;          // ready for the next launch
 }
 
+// ------------------------------------------------------------- greedy pick
+// next_ids[b] = argmax over the vocabulary of logits row b, the vocabulary
+// split over `world` ranks (this rank holds ids [rank*V, (rank+1)*V)).  One
+// CTA per row: thread-level then warp-level (max, lowest index on ties), then
+// for world > 1 thread 0 stores (value, global id) as two epoch-flagged
+// 64-bit words into slot `rank` of every rank's pick buffer (peer memory) and
+// reads every rank's pair from its own buffer (bounded wait for the epoch);
+// the largest value wins, the lowest rank on ties (= the lowest id, torch's
+// first-index rule).
+__device__ __forceinline__ void st_sys_u64(uint64_t *p, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_sys_u64(const uint64_t *p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+struct PickPeers {
+    uint64_t *slot[8];                 // rank p's pick buffer, this rank's slot ([B][2] words)
+};
+
+__device__ __forceinline__ bool pick_better(float v, int64_t i, float bv, int64_t bi) {
+    return v > bv || (v == bv && i < bi) || (bv != bv && v == v);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(1024) k_greedy_pick(const T *logits, int64_t V, int64_t ld, int rank, int world,
+                                                     const PickPeers pp, const uint64_t *local, const uint32_t *epoch,
+                                                     int64_t *next_ids, uint32_t *status) {
+    __shared__ float sv[32];
+    __shared__ int64_t si[32];
+    pdl_launch_dependents();
+    pdl_wait();
+    const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const T *row = logits + (int64_t)b * ld;
+    float bv = -INFINITY;
+    int64_t bi = INT64_MAX;
+    for (int64_t i = tid; i < V; i += blockDim.x) {
+        const float v = to_f32<T>(row[i]);
+        if (pick_better(v, i, bv, bi)) { bv = v; bi = i; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float v = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int64_t i = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (pick_better(v, i, bv, bi)) { bv = v; bi = i; }
+    }
+    if (lane == 0) { sv[w] = bv; si[w] = bi; }
+    __syncthreads();
+    if (tid != 0) return;
+    bv = sv[0]; bi = si[0];
+    for (int i = 1; i < (int)(blockDim.x >> 5); ++i)
+        if (pick_better(sv[i], si[i], bv, bi)) { bv = sv[i]; bi = si[i]; }
+    int64_t id = bi + (int64_t)rank * V;
+    if (world > 1) {
+        const uint64_t ep = (uint64_t)*epoch << 32;
+        for (int p = 0; p < world; ++p) {
+            st_sys_u64(pp.slot[p] + 2 * b, ep | __float_as_uint(bv));
+            st_sys_u64(pp.slot[p] + 2 * b + 1, ep | (uint32_t)id);
+        }
+        float gv = -INFINITY;
+        int64_t gid = INT64_MAX;
+        const uint64_t t0 = global_timer_ns();
+        for (int p = 0; p < world; ++p) {
+            const uint64_t *q = local + ((int64_t)p * gridDim.x + b) * 2;
+            uint64_t a, c;
+            while (true) {
+                a = ld_sys_u64(q);
+                c = ld_sys_u64(q + 1);
+                if ((a >> 32) == (ep >> 32) && (c >> 32) == (ep >> 32)) break;
+                if (global_timer_ns() - t0 > kWaitNs) {
+                    report(status, CBQ_FLAG_TIMEOUT, (uint32_t)b);
+                    return;                                // next_ids[b] keeps its old value
+                }
+                __nanosleep(32);
+            }
+            const float v = __uint_as_float((uint32_t)a);
+            const int64_t i = (int64_t)(uint32_t)c;
+            if (pick_better(v, i, gv, gid)) { gv = v; gid = i; }
+        }
+        id = gid;
+    }
+    next_ids[b] = id;
+}
+
 }  // namespace
 
 // ------------------------------------------------------------------- C ABI
+
+extern "C" int cbq_greedy_pick(const void *logits_dev, int dtype, int64_t B, int64_t V, int64_t ld, int rank,
+                               int world, void *const *slot_dev, const void *local_slots_dev,
+                               const uint32_t *epoch_dev, int64_t *next_ids_dev, uint32_t *status_dev,
+                               void *stream) {
+    if (B < 0 || V < 1 || ld < V || world < 1 || world > 8 || rank < 0 || rank >= world ||
+        (dtype != CBQ_F32 && dtype != CBQ_BF16))
+        return CBQ_ERR_ARG;
+    if (B == 0) return CBQ_OK;
+    if (!logits_dev || !next_ids_dev || B > 65535 || (int64_t)V * world >= (1ll << 32)) return CBQ_ERR_ARG;
+    PickPeers pp{};
+    if (world > 1) {
+        if (!slot_dev || !local_slots_dev || !epoch_dev) return CBQ_ERR_ARG;
+        for (int p = 0; p < world; ++p) {
+            if (!slot_dev[p] || (reinterpret_cast<uintptr_t>(slot_dev[p]) & 7)) return CBQ_ERR_ARG;
+            pp.slot[p] = static_cast<uint64_t *>(slot_dev[p]);
+        }
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (dtype == CBQ_F32)
+        CBQ_CUDA_TRY(cbq_host::launch_pdl(k_greedy_pick<float>, dim3((unsigned)B), dim3(1024), 0, s,
+                                          static_cast<const float *>(logits_dev), V, ld, rank, world, pp,
+                                          static_cast<const uint64_t *>(local_slots_dev), epoch_dev, next_ids_dev,
+                                          status_dev));
+    else
+        CBQ_CUDA_TRY(cbq_host::launch_pdl(k_greedy_pick<__nv_bfloat16>, dim3((unsigned)B), dim3(1024), 0, s,
+                                          static_cast<const __nv_bfloat16 *>(logits_dev), V, ld, rank, world, pp,
+                                          static_cast<const uint64_t *>(local_slots_dev), epoch_dev, next_ids_dev,
+                                          status_dev));
+    return CBQ_OK;
+}
 
 extern "C" int cbq_rmsnorm(void *x_dev, const void *add_dev, int dtype, int64_t rows, int64_t n,
                            const float *weight_dev, float eps, void *out_dev, void *stream) {

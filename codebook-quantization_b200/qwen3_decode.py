@@ -73,7 +73,9 @@ class _PeerAllReduce:
         # data bits + the epoch, two bf16 or one fp32 value per word
         self.flag_bytes = dec.B * dec.cfg.hidden * (4 if self.elem == 2 else 8)
         self.flag_off = data + counters
-        total = self.flag_off + sites * W * self.flag_bytes
+        # greedy pick: per rank, [W][B][2] 64-bit words (value, id) flagged with the epoch
+        self.pick_off = self.flag_off + sites * W * self.flag_bytes
+        total = self.pick_off + W * dec.B * 16
         self.buf = symm.empty(total, dtype=torch.uint8, device=dec.dev)
         self.buf.zero_()
         self.hdl = symm.rendezvous(self.buf, dec.group)
@@ -89,6 +91,8 @@ class _PeerAllReduce:
             self.counts.append((P * W)(*[ptrs[p] + data + (i * W + r) * 4 for p in range(W)]))
             self.flagged.append((P * W)(*[ptrs[p] + self.flag_off + (i * W + r) * self.flag_bytes
                                           for p in range(W)]))
+        self.pick = (P * W)(*[ptrs[p] + self.pick_off + r * dec.B * 16 for p in range(W)])
+        self.local_pick = self.local + self.pick_off
         torch.cuda.synchronize(dec.dev)
         dist.barrier(group=dec.group)
 
@@ -418,6 +422,17 @@ class Qwen3Decoder:
 
     def _finish(self, logits):
         self.logits = logits
+        if self.fused and (self.world == 1 or self.peer is not None) and logits.is_contiguous():
+            # one launch: the row argmax, exchanged between ranks through
+            # epoch-flagged words in peer memory (cbq_greedy_pick)
+            pr = self.peer
+            code = _lib.CBQ_BF16 if logits.dtype == torch.bfloat16 else _lib.CBQ_F32
+            lg = logits if logits.dtype in (torch.bfloat16, torch.float32) else logits.float()
+            _lib.call("cbq_greedy_pick", lg.data_ptr(), code, self.B, lg.shape[-1], lg.shape[-1], self.rank,
+                      self.world, None if pr is None else pr.pick, None if pr is None else pr.local_pick,
+                      None if pr is None else pr.epoch.data_ptr(), self.next_ids.data_ptr(),
+                      None if pr is None else pr.status.data_ptr(), device_stream(self.dev))
+            return
         val, idx = logits.float().max(dim=-1)
         idx = idx + self.rank * self.vocab_local
         if self.world > 1:
@@ -435,15 +450,16 @@ class Qwen3Decoder:
         if not self.fused:
             return 1 + 7 * n + 1          # embedding, 7 linears per layer, lm_head
         attn = 1 if self.fuse_rope else 2
-        if self.prenorm or self.peer_prenorm:   # embedding, 5 per layer (norms inside the GEMVs), lm_head
-            return 1 + 5 * n + 1
+        if self.prenorm or self.peer_prenorm:   # embedding, 5 per layer (norms inside the GEMVs), lm_head, pick
+            return 1 + 5 * n + 2
+        pick = 1 if (self.world == 1 or self.peer is not None) else 0   # cbq_greedy_pick
         if self.w.huffman or self.B > 2:  # one launch per linear, separate RMSNorms
             per = 3 + attn + 1 + 2 + 1 + 2
         elif (self.world == 1 or self.peer is not None) and self.fuse_norm:
             per = 4 + attn                # q/k/v, attention, o (+norm), gate/up, down (+norm)
         else:
             per = 6 + attn                # the same with two RMSNorm launches (after NCCL at TP > 1)
-        return 2 + per * n + 1            # embedding + first RMSNorm, the layers, lm_head
+        return 2 + per * n + 1 + pick     # embedding + first RMSNorm, the layers, lm_head
 
     def layer_launches(self) -> str:
         """The launches of one decoder layer of the step, in order."""

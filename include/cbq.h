@@ -449,6 +449,21 @@ int cbq_rmsnorm_allreduce(void *x_dev, const void *slots_dev, const uint32_t *co
                           int64_t n, const float *weight_dev, float eps, void *out_dev,
                           uint32_t *status_dev, void *stream);
 
+/* Greedy next token of B logits rows [B, ld] (this rank's V vocabulary
+ * entries, ids rank*V .. rank*V + V - 1): the largest logit, the lowest id on
+ * ties (torch's max), written to next_ids_dev[b] (int64).  world > 1: each
+ * rank stores its (value, id) pair as two epoch-flagged 64-bit words into
+ * slot `rank` of every rank's pick buffer (slot_dev[p]: rank p's buffer at
+ * this rank's slot, [B][2] words; local_slots_dev: this rank's buffer,
+ * [world][B][2] words) and takes the best of the world pairs it reads back
+ * (bounded wait for *epoch_dev; on timeout CBQ_FLAG_TIMEOUT in status_dev and
+ * the row keeps its previous id).  Replaces the all-gather of (max, index)
+ * pairs and the torch reductions around it.  No counterpart in the reference
+ * (HF's generate picks on the host framework's side). */
+int cbq_greedy_pick(const void *logits_dev, int dtype, int64_t B, int64_t V, int64_t ld, int rank, int world,
+                    void *const *slot_dev, const void *local_slots_dev, const uint32_t *epoch_dev,
+                    int64_t *next_ids_dev, uint32_t *status_dev, void *stream);
+
 /* The attention block's element-wise part for the token at position *pos_dev
  * (device int64): per-head RMSNorm of q [B, Hq*d] and k [B, Hkv*d] (weights
  * fp32 [d] or NULL = 1), rotary embedding with cos/sin tables (fp32

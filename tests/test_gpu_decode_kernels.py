@@ -398,3 +398,44 @@ def test_flagged_peer_slots_feed_the_consuming_gemv(dt):
         assert torch.equal(x, want), step
         assert torch.equal(out, ref), step
         resid = x.clone()
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+def test_greedy_pick_equals_torch_argmax(dt):
+    """cbq_greedy_pick on one GPU: the first index of the row maximum, like
+    torch's max, including ties; and the two-'rank' exchange (both ranks'
+    pick buffers on this GPU) gives the global argmax over both halves."""
+    import ctypes as ct
+    dev = need_cuda()
+    B, V = 3, 151936
+    lg = torch.randn(B, V, device=dev).to(dt)
+    lg[1, 777] = lg[1, 99999] = 1e4                        # a tie: the first index wins
+    ids = torch.full((B,), -1, dtype=torch.int64, device=dev)
+    code = L.CBQ_BF16 if dt == torch.bfloat16 else L.CBQ_F32
+    st = torch.cuda.current_stream(dev).cuda_stream
+    L.call("cbq_greedy_pick", lg.data_ptr(), code, B, V, V, 0, 1, None, None, None, ids.data_ptr(), None, st)
+    torch.cuda.synchronize()
+    assert torch.equal(ids, lg.float().max(dim=-1).indices)
+    # two ranks: rank 1's pair is already in rank 0's pick buffer (written
+    # here as rank 1's launch would), so rank 0's launch finds every pair it
+    # waits for; it publishes its own pair into both buffers
+    W, Vh = 2, V // 2
+    bufs = torch.zeros(W, W * B * 2, dtype=torch.int64, device=dev)
+    epoch = torch.full((1,), 5, dtype=torch.int32, device=dev)
+    status = torch.tensor([0, -1, 0, 0], dtype=torch.int32, device=dev)
+    v1, i1 = lg[:, Vh:].float().max(dim=-1)
+    words = torch.stack([(v1.view(torch.int32).to(torch.int64) & 0xFFFFFFFF) | (5 << 32),
+                         (i1 + Vh) | (5 << 32)], dim=1).reshape(-1)
+    bufs[0, B * 2:].copy_(words)
+    out = torch.full((B,), -1, dtype=torch.int64, device=dev)
+    part = lg[:, :Vh].contiguous()
+    P = ct.c_void_p
+    ptrs = (P * W)(*[bufs[p].data_ptr() for p in range(W)])           # slot 0 of each buffer
+    L.call("cbq_greedy_pick", part.data_ptr(), code, B, Vh, Vh, 0, W, ptrs, bufs[0].data_ptr(),
+           epoch.data_ptr(), out.data_ptr(), status.data_ptr(), st)
+    torch.cuda.synchronize()
+    assert int(status[0].item()) == 0
+    assert torch.equal(out, lg.float().max(dim=-1).indices)
+    v0, i0 = lg[:, :Vh].float().max(dim=-1)                           # what rank 0 published
+    got = bufs[1, :B * 2].view(B, 2)
+    assert torch.equal(got[:, 1] & 0xFFFFFFFF, i0) and bool(((got >> 32) == 5).all())
