@@ -354,6 +354,17 @@ __device__ __forceinline__ uint32_t gv_field(const uint32_t (&w)[NF * BITS / 32 
     return v & mask;
 }
 
+// a0 = fma(x0, v0, a0), a1 = fma(x1, v1, a1) in one paired fp32 instruction.
+__device__ __forceinline__ void ffma2(float &a0, float &a1, float x0, float x1, float v0, float v1) {
+    asm("{.reg .b64 A, X, V;\n\t"
+        "mov.b64 A, {%0, %1};\n\t"
+        "mov.b64 X, {%2, %3};\n\t"
+        "mov.b64 V, {%4, %5};\n\t"
+        "fma.rn.f32x2 A, X, V, A;\n\t"
+        "mov.b64 {%0, %1}, A;\n\t}"
+        : "+f"(a0), "+f"(a1) : "f"(x0), "f"(x1), "f"(v0), "f"(v1));
+}
+
 __device__ __forceinline__ float gv_lds(uint32_t addr) {
     float v;
     asm("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
@@ -438,29 +449,39 @@ __device__ __forceinline__ void gv_st8(XT *p, const float (&v)[8]) {
     }
 }
 
-// Eight activations k0..k0+7 of token t from every rank's flagged slot
-// (GemvPeers::ll_epoch): the 64-bit words are read until each carries this
-// step's epoch (bounded; on giving up sets *late, records CBQ_FLAG_TIMEOUT
-// and returns false).  Slot p of the consumer's buffer is ar_slots + p *
-// ntok * K words (fp32) or K/2 words (bf16) per token.
+// Adds, in rank order, every rank's values of activations k0..k0+7 of token t
+// from its flagged slot (GemvPeers::ll_epoch) to sum: the 64-bit words are
+// read, four ranks' at a time with all their loads issued together, until
+// each carries this step's epoch (bounded; on giving up sets *late, records
+// CBQ_FLAG_TIMEOUT and returns false).  Slot p of the consumer's buffer is
+// ar_slots + p * ntok * K words (fp32) or K/2 words (bf16) per token.
 template <typename XT>
-__device__ __forceinline__ bool gv_ll_read8(const GemvArgs &a, int t, int k0, float (&sp)[kGvMaxPeers][8],
-                                            int *late) {
+__device__ __forceinline__ bool gv_ll_sum8(const GemvArgs &a, int t, int k0, float (&sum)[8], int *late) {
     constexpr bool kBf = !std::is_same<XT, float>::value;
     constexpr int NWD = kBf ? 4 : 8;                        // words per 8 activations
+    constexpr int PG = 4;                                   // ranks per batch of loads
     const int64_t per_tok = kBf ? a.K / 2 : a.K;
     const uint64_t *base = static_cast<const uint64_t *>(a.ar_slots);
     const uint32_t ep = *a.ar_epoch;
     uint64_t t0 = 0;
-    for (int p = 0; p < a.ar_world; ++p) {
-        const uint64_t *w = base + ((int64_t)p * a.ntok + t) * per_tok + (kBf ? k0 / 2 : k0);
-        uint64_t v[NWD];
+    for (int p0 = 0; p0 < a.ar_world; p0 += PG) {
+        uint64_t v[PG][NWD];
         while (true) {
-#pragma unroll
-            for (int i = 0; i < NWD; ++i) v[i] = ld_relaxed_sys_u64(w + i);
             bool ok = true;
 #pragma unroll
-            for (int i = 0; i < NWD; ++i) ok &= (uint32_t)(v[i] >> 32) == ep;
+            for (int g = 0; g < PG; ++g) {
+                if (p0 + g < a.ar_world) {
+                    const uint64_t *w = base + ((int64_t)(p0 + g) * a.ntok + t) * per_tok + (kBf ? k0 / 2 : k0);
+#pragma unroll
+                    for (int i = 0; i < NWD; ++i) v[g][i] = ld_relaxed_sys_u64(w + i);
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < PG; ++g)
+                if (p0 + g < a.ar_world) {
+#pragma unroll
+                    for (int i = 0; i < NWD; ++i) ok &= (uint32_t)(v[g][i] >> 32) == ep;
+                }
             if (ok) break;
             if (*(volatile int *)late) return false;         // this CTA, or an earlier call, gave up
             if (t0 == 0) t0 = global_timer_ns();
@@ -471,13 +492,17 @@ __device__ __forceinline__ bool gv_ll_read8(const GemvArgs &a, int t, int k0, fl
             __nanosleep(32);
         }
 #pragma unroll
-        for (int i = 0; i < NWD; ++i) {
-            const uint32_t d = (uint32_t)v[i];
-            if (kBf) {
-                sp[p][2 * i] = __uint_as_float(d << 16);
-                sp[p][2 * i + 1] = __uint_as_float(d & 0xffff0000u);
-            } else {
-                sp[p][i] = __uint_as_float(d);
+        for (int g = 0; g < PG; ++g) {
+            if (p0 + g >= a.ar_world) break;
+#pragma unroll
+            for (int i = 0; i < NWD; ++i) {
+                const uint32_t d = (uint32_t)v[g][i];
+                if (kBf) {
+                    sum[2 * i] += __uint_as_float(d << 16);
+                    sum[2 * i + 1] += __uint_as_float(d & 0xffff0000u);
+                } else {
+                    sum[i] += __uint_as_float(d);
+                }
             }
         }
     }
@@ -536,31 +561,22 @@ __device__ __forceinline__ bool gv_prologue(const GemvArgs &a, float (&scale)[TB
             for (int k0 = tid * 8; k0 < a.K; k0 += NT * 8) {
                 float v[8];
                 if (a.ar_on) {
-                    float r[8], sum[8], sp[kGvMaxPeers][8];
+                    float r[8], sum[8];
                     gv_ld8<XT>(res + row + k0, false, r);
-                    if (a.ar_ll) {
-                        // on giving up the values are zeros; every thread still
-                        // reaches the barriers below, and the call reports it
-                        if (!gv_ll_read8<XT>(a, t, k0, sp, late)) {
-#pragma unroll
-                            for (int p = 0; p < kGvMaxPeers; ++p)
-#pragma unroll
-                                for (int e = 0; e < 8; ++e) sp[p][e] = 0.f;
-                        }
-                    } else {
-#pragma unroll
-                        for (int p = 0; p < kGvMaxPeers; ++p)
-                            if (p < a.ar_world)
-                                gv_ld8<XT>(slots + ((int64_t)p * a.ntok + t) * a.K + k0, true, sp[p]);
-                    }
 #pragma unroll
                     for (int e = 0; e < 8; ++e) sum[e] = 0.f;
+                    if (a.ar_ll) {
+                        // on giving up the values are garbage; every thread
+                        // still reaches the barriers below, and the call reports it
+                        gv_ll_sum8<XT>(a, t, k0, sum, late);
+                    } else {
+                        for (int p = 0; p < a.ar_world; ++p) {       // rank order
+                            float sp[8];
+                            gv_ld8<XT>(slots + ((int64_t)p * a.ntok + t) * a.K + k0, true, sp);
 #pragma unroll
-                    for (int p = 0; p < kGvMaxPeers; ++p)
-                        if (p < a.ar_world) {
-#pragma unroll
-                            for (int e = 0; e < 8; ++e) sum[e] += sp[p][e];
+                            for (int e = 0; e < 8; ++e) sum[e] += sp[e];
                         }
+                    }
 #pragma unroll
                     for (int e = 0; e < 8; ++e)
                         v[e] = to_f32<XT>(from_f32<XT>(r[e] + to_f32<XT>(from_f32<XT>(sum[e]))));
@@ -790,24 +806,27 @@ __global__ void __launch_bounds__(kGvWarps * 32, 1) k_gemv_fixed(const GemvArgs 
             gv_load_share<BITS, NF>(slot_words(slot), w);
             if (two) gv_load_share<BITS, NF>(slot_words(slot2), w2);
         }
+        // Indices q and q + 1 go to the even / odd accumulators, two fp32 FMAs
+        // in one paired instruction (fma.rn.f32x2: each lane rounds exactly as
+        // fmaf does).
         if (live) {
             if (two) {
 #pragma unroll
-                for (int q = 0; q < NF; ++q) {
-                    const float v = gather(gv_field<BITS, NF>(w, q));
-                    const float v2 = gather(gv_field<BITS, NF>(w2, q));
+                for (int q = 0; q < NF; q += 2) {
+                    const float v0 = gather(gv_field<BITS, NF>(w, q)), v1 = gather(gv_field<BITS, NF>(w, q + 1));
+                    const float u0 = gather(gv_field<BITS, NF>(w2, q)), u1 = gather(gv_field<BITS, NF>(w2, q + 1));
 #pragma unroll
                     for (int t = 0; t < TB; ++t) {
-                        acc[0][q & 1][t] = fmaf(xr[t][q], v, acc[0][q & 1][t]);
-                        acc[1][q & 1][t] = fmaf(xr[t][q], v2, acc[1][q & 1][t]);
+                        ffma2(acc[0][0][t], acc[0][1][t], xr[t][q], xr[t][q + 1], v0, v1);
+                        ffma2(acc[1][0][t], acc[1][1][t], xr[t][q], xr[t][q + 1], u0, u1);
                     }
                 }
             } else {
 #pragma unroll
-                for (int q = 0; q < NF; ++q) {
-                    const float v = gather(gv_field<BITS, NF>(w, q));
+                for (int q = 0; q < NF; q += 2) {
+                    const float v0 = gather(gv_field<BITS, NF>(w, q)), v1 = gather(gv_field<BITS, NF>(w, q + 1));
 #pragma unroll
-                    for (int t = 0; t < TB; ++t) acc[0][q & 1][t] = fmaf(xr[t][q], v, acc[0][q & 1][t]);
+                    for (int t = 0; t < TB; ++t) ffma2(acc[0][0][t], acc[0][1][t], xr[t][q], xr[t][q + 1], v0, v1);
                 }
             }
         }
