@@ -354,17 +354,6 @@ __device__ __forceinline__ uint32_t gv_field(const uint32_t (&w)[NF * BITS / 32 
     return v & mask;
 }
 
-// a0 = fma(x0, v0, a0), a1 = fma(x1, v1, a1) in one paired fp32 instruction.
-__device__ __forceinline__ void ffma2(float &a0, float &a1, float x0, float x1, float v0, float v1) {
-    asm("{.reg .b64 A, X, V;\n\t"
-        "mov.b64 A, {%0, %1};\n\t"
-        "mov.b64 X, {%2, %3};\n\t"
-        "mov.b64 V, {%4, %5};\n\t"
-        "fma.rn.f32x2 A, X, V, A;\n\t"
-        "mov.b64 {%0, %1}, A;\n\t}"
-        : "+f"(a0), "+f"(a1) : "f"(x0), "f"(x1), "f"(v0), "f"(v1));
-}
-
 __device__ __forceinline__ float gv_lds(uint32_t addr) {
     float v;
     asm("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
@@ -806,27 +795,24 @@ __global__ void __launch_bounds__(kGvWarps * 32, 1) k_gemv_fixed(const GemvArgs 
             gv_load_share<BITS, NF>(slot_words(slot), w);
             if (two) gv_load_share<BITS, NF>(slot_words(slot2), w2);
         }
-        // Indices q and q + 1 go to the even / odd accumulators, two fp32 FMAs
-        // in one paired instruction (fma.rn.f32x2: each lane rounds exactly as
-        // fmaf does).
         if (live) {
             if (two) {
 #pragma unroll
-                for (int q = 0; q < NF; q += 2) {
-                    const float v0 = gather(gv_field<BITS, NF>(w, q)), v1 = gather(gv_field<BITS, NF>(w, q + 1));
-                    const float u0 = gather(gv_field<BITS, NF>(w2, q)), u1 = gather(gv_field<BITS, NF>(w2, q + 1));
+                for (int q = 0; q < NF; ++q) {
+                    const float v = gather(gv_field<BITS, NF>(w, q));
+                    const float v2 = gather(gv_field<BITS, NF>(w2, q));
 #pragma unroll
                     for (int t = 0; t < TB; ++t) {
-                        ffma2(acc[0][0][t], acc[0][1][t], xr[t][q], xr[t][q + 1], v0, v1);
-                        ffma2(acc[1][0][t], acc[1][1][t], xr[t][q], xr[t][q + 1], u0, u1);
+                        acc[0][q & 1][t] = fmaf(xr[t][q], v, acc[0][q & 1][t]);
+                        acc[1][q & 1][t] = fmaf(xr[t][q], v2, acc[1][q & 1][t]);
                     }
                 }
             } else {
 #pragma unroll
-                for (int q = 0; q < NF; q += 2) {
-                    const float v0 = gather(gv_field<BITS, NF>(w, q)), v1 = gather(gv_field<BITS, NF>(w, q + 1));
+                for (int q = 0; q < NF; ++q) {
+                    const float v = gather(gv_field<BITS, NF>(w, q));
 #pragma unroll
-                    for (int t = 0; t < TB; ++t) ffma2(acc[0][0][t], acc[0][1][t], xr[t][q], xr[t][q + 1], v0, v1);
+                    for (int t = 0; t < TB; ++t) acc[0][q & 1][t] = fmaf(xr[t][q], v, acc[0][q & 1][t]);
                 }
             }
         }
