@@ -251,10 +251,24 @@ __global__ void __launch_bounds__(D) k_attn_decode(const T *q, T *k_cache, T *v_
     __shared__ float qs[ROPE ? G : 1][D];         // ROPE: the rotated queries
     __shared__ int last;
     pdl_launch_dependents();
-    pdl_wait();
     const int S = sp.S, cmax = sp.cmax;
     const int bg = blockIdx.x / S, s = blockIdx.x - (blockIdx.x / S) * S;
     const int b = bg / Hkv, g = bg - b * Hkv;
+    if (threadIdx.x == 0) {
+        // Before waiting for the kernel that wrote q/k/v: start the cache rows
+        // of the earlier positions on their way into L2 (a hint only: the
+        // position read here may be stale, the range is clamped to the cache).
+        const int64_t p0 = min(max(*(volatile const int64_t *)pos_dev, (int64_t)0), L);
+        const int64_t c0 = (p0 + 1 + S - 1) / S;
+        const int64_t a0 = min((int64_t)s * c0, p0), a1 = min(a0 + c0, p0);
+        if (a1 > a0) {
+            const uint32_t bytes = (uint32_t)((a1 - a0) * D * sizeof(T));
+            const int64_t off = ((int64_t)bg * L + a0) * D;
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(k_cache + off), "r"(bytes) : "memory");
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(v_cache + off), "r"(bytes) : "memory");
+        }
+    }
+    pdl_wait();
     const int64_t pos = *pos_dev;
     int64_t n = min(pos + 1, L);                       // keys 0..pos (none if pos < 0)
     if (ROPE && pos >= L) n = 0;
