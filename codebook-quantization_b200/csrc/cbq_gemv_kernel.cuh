@@ -675,24 +675,48 @@ __global__ void __launch_bounds__(kGvWarps * 32, 1) k_gemv_fixed(const GemvArgs 
         if (++irl == nrows) { irl = 0; ++is; }
         if (++islot == kGvSlots) islot = 0;
     };
-    if (lane == 0) {
-        for (int s = 0; s < kGvSlots; ++s) mbar_init(&bars[s], 1);
-        mbar_fence_init();
-        for (int i = 0; i < n && i < kGvSlots; ++i) issue_next();
-    }
-
     // codebook: replicated head, then the single copy (padded for b <= 14).
     // One load per entry; a head row (32 copies, 128 B) is written as eight
     // 16-byte stores whose order is rotated by lane so that the eight lanes
-    // of each store phase hit distinct banks.
-    // All loads of a pass are issued before any store, so the pass costs one
-    // global-memory latency.
+    // of each store phase hit distinct banks.  The loads of the first pass
+    // (the whole table for codebooks of up to 4096 + 12288 entries) are
+    // issued before the first stream copies, which would otherwise queue
+    // ahead of them, and before any store: the table costs one latency.
     {
         const uint32_t H = a.H, NP = a.NP;
         const int cmax = a.C - 1;
         constexpr int kT = kGvWarps * 32;
-        constexpr int kBatch = 8;
-        for (uint32_t e0 = 0; e0 < H; e0 += kT * kBatch) {
+        constexpr int kBatch = 8, kTB = 24;
+        float vh[kBatch], vt[kTB];
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+            const uint32_t e = j * kT + tid;
+            vh[j] = e < H ? __ldg(a.codebook + min((int)e, cmax)) : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < kTB; ++j) {
+            const uint32_t c = H + j * kT + tid;
+            vt[j] = c < NP ? __ldg(a.codebook + min((int)c, cmax)) : 0.f;
+        }
+        if (lane == 0) {
+            for (int s = 0; s < kGvSlots; ++s) mbar_init(&bars[s], 1);
+            mbar_fence_init();
+            for (int i = 0; i < n && i < kGvSlots; ++i) issue_next();
+        }
+        auto put_head = [&](uint32_t e, float v) {
+            const float4 v4 = make_float4(v, v, v, v);
+            float4 *row = reinterpret_cast<float4 *>(cbs + (size_t)e * 128);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) row[(q + lane) & 7] = v4;
+        };
+        float *tw = reinterpret_cast<float *>(cbs + (size_t)H * 128);
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j)
+            if (j * kT + tid < H) put_head(j * kT + tid, vh[j]);
+#pragma unroll
+        for (int j = 0; j < kTB; ++j)
+            if (H + j * kT + tid < NP) tw[j * kT + tid] = vt[j];
+        for (uint32_t e0 = kT * kBatch; e0 < H; e0 += kT * kBatch) {     // larger tables
             float v[kBatch];
 #pragma unroll
             for (int j = 0; j < kBatch; ++j) {
@@ -700,19 +724,10 @@ __global__ void __launch_bounds__(kGvWarps * 32, 1) k_gemv_fixed(const GemvArgs 
                 v[j] = e < H ? __ldg(a.codebook + min((int)e, cmax)) : 0.f;
             }
 #pragma unroll
-            for (int j = 0; j < kBatch; ++j) {
-                const uint32_t e = e0 + j * kT + tid;
-                if (e < H) {
-                    const float4 v4 = make_float4(v[j], v[j], v[j], v[j]);
-                    float4 *row = reinterpret_cast<float4 *>(cbs + (size_t)e * 128);
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) row[(q + lane) & 7] = v4;
-                }
-            }
+            for (int j = 0; j < kBatch; ++j)
+                if (e0 + j * kT + tid < H) put_head(e0 + j * kT + tid, v[j]);
         }
-        float *tw = reinterpret_cast<float *>(cbs + (size_t)H * 128);
-        constexpr int kTB = 24;
-        for (uint32_t c0 = H; c0 < NP; c0 += kT * kTB) {
+        for (uint32_t c0 = H + kT * kTB; c0 < NP; c0 += kT * kTB) {
             float v[kTB];
 #pragma unroll
             for (int j = 0; j < kTB; ++j) {
