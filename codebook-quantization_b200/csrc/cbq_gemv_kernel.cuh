@@ -440,7 +440,8 @@ __device__ __forceinline__ void gv_st8(XT *p, const float (&v)[8]) {
 
 // Adds, in rank order, every rank's values of activations k0..k0+7 of token t
 // from its flagged slot (GemvPeers::ll_epoch) to sum: the 64-bit words are
-// read, four ranks' at a time with all their loads issued together, until
+// read, eight ranks' (bf16) or four ranks' (fp32) at a time with all their
+// loads issued together, until
 // each carries this step's epoch (bounded; on giving up sets *late, records
 // CBQ_FLAG_TIMEOUT and returns false).  Slot p of the consumer's buffer is
 // ar_slots + p * ntok * K words (fp32) or K/2 words (bf16) per token.
@@ -448,7 +449,7 @@ template <typename XT>
 __device__ __forceinline__ bool gv_ll_sum8(const GemvArgs &a, int t, int k0, float (&sum)[8], int *late) {
     constexpr bool kBf = !std::is_same<XT, float>::value;
     constexpr int NWD = kBf ? 4 : 8;                        // words per 8 activations
-    constexpr int PG = 4;                                   // ranks per batch of loads
+    constexpr int PG = kBf ? 8 : 4;                         // ranks per batch of loads (64 registers)
     const int64_t per_tok = kBf ? a.K / 2 : a.K;
     const uint64_t *base = static_cast<const uint64_t *>(a.ar_slots);
     const uint32_t ep = *a.ar_epoch;

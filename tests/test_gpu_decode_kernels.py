@@ -355,18 +355,20 @@ def test_residual_norm_launch_equals_gemv_then_rmsnorm(dt, T, M, K):
         assert int(arrive.item()) == 0
 
 
+@pytest.mark.parametrize("world", [2, 5, 8])
 @pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
-def test_flagged_peer_slots_feed_the_consuming_gemv(dt):
-    """Two row-parallel partial products written as epoch-flagged slot words
-    (cbq_linear_fixed_peer_flagged, one 'rank' each, both slots on this GPU)
-    and consumed by cbq_linear_fixed_multi_allreduce_norm: the residual it
-    writes is round(resid + round(p0 + p1)) in rank order, and its GEMV equals
+def test_flagged_peer_slots_feed_the_consuming_gemv(dt, world):
+    """Row-parallel partial products written as epoch-flagged slot words
+    (cbq_linear_fixed_peer_flagged, one 'rank' each, every slot on this GPU,
+    each producer finished before the consumer starts) and consumed by
+    cbq_linear_fixed_multi_allreduce_norm: the residual it writes is
+    round(resid + round(p0 + p1 + ...)) in rank order, and its GEMV equals
     RMSNorm of that residual through cbq_linear_fixed_multi_norm; a second
     step (next epoch) over the same slots gives the same."""
     import ctypes as ct
     dev = need_cuda()
-    H, Kp, T, world = 1024, 512, 1, 2
-    o0, o1 = _mats(dev, [H, H], Kp, seed=21)
+    H, Kp, T = 1024, 512, 1
+    os_ = _mats(dev, [H] * world, Kp, seed=21)
     (g,) = _mats(dev, [768], H, seed=22)
     code = L.CBQ_BF16 if dt == torch.bfloat16 else L.CBQ_F32
     st = torch.cuda.current_stream(dev).cuda_stream
@@ -377,9 +379,8 @@ def test_flagged_peer_slots_feed_the_consuming_gemv(dt):
     resid = (torch.randn(T, H, device=dev) * 2).to(dt)
     for step in range(2):
         epoch.add_(1)
-        a0 = torch.randn(T, Kp, device=dev).to(dt)
-        a1 = torch.randn(T, Kp, device=dev).to(dt)
-        for r, (m, a) in enumerate(((o0, a0), (o1, a1))):
+        acts = [torch.randn(T, Kp, device=dev).to(dt) for _ in range(world)]
+        for r, (m, a) in enumerate(zip(os_, acts)):
             ptrs = (ct.c_void_p * 1)(slots.data_ptr() + r * per)
             rc = L.lib().cbq_linear_fixed_peer_flagged(a.data_ptr(), code, T, Kp, m.packed.data_ptr(), m.nbytes,
                                                        m.codebook.data_ptr(), m.C, m.bits, H, Kp, None, 1, ptrs,
@@ -389,8 +390,10 @@ def test_flagged_peer_slots_feed_the_consuming_gemv(dt):
         out = torch.empty(T, 768, device=dev, dtype=dt)
         ar = (world, resid, slots.data_ptr(), None, epoch.data_ptr(), H, status.data_ptr())
         assert G.linear_fixed_multi([g], x, [out], norm=(None, 1e-6), allreduce=ar)
-        p0, p1 = o0(a0), o1(a1)
-        want = (resid.float() + (p0.float() + p1.float()).to(dt).float()).to(dt)
+        tot = torch.zeros(T, H, device=dev)
+        for m, a in zip(os_, acts):                    # rank order
+            tot = tot + m(a).float()
+        want = (resid.float() + tot.to(dt).float()).to(dt)
         ref = torch.empty_like(out)
         assert G.linear_fixed_multi([g], want, [ref], norm=(None, 1e-6))
         torch.cuda.synchronize()
