@@ -41,6 +41,14 @@ bool pdl_enabled() {
     return on;
 }
 
+bool attn_cluster_enabled() {
+    static const bool on = [] {
+        const char *v = std::getenv("CBQ_ATTN_CLUSTER");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
 }  // namespace cbq_host
 
 extern "C" const char *cbq_status_string(int status) {

@@ -150,6 +150,7 @@ int sm_count();           // SMs of the current device (cached per device)
 int max_smem_optin();     // opt-in dynamic shared memory per block
 inline int64_t align_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
 bool pdl_enabled();       // programmatic dependent launch (CBQ_PDL=0 in the environment turns it off)
+bool attn_cluster_enabled();   // split attention as clusters (CBQ_ATTN_CLUSTER=0 turns it off)
 
 // Launch `kern` on `s` with the programmatic-stream-serialization attribute
 // (see pdl_wait above); plain stream order when PDL is off.
@@ -166,6 +167,28 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
+// launch_pdl with the grid tiled into thread-block clusters of `cluster`
+// consecutive CTAs (x dimension).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, unsigned cluster,
+                               cudaStream_t s, Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 }  // namespace cbq_host

@@ -237,7 +237,22 @@ struct AttnSplit {
     int cmax;                          // score slots per head in shared memory (>= ceil(n / S))
     float *part;                       // S > 1: [B * Hkv][S][G * D + 2 * G] fp32
     uint32_t *count;                   // S > 1: [B * Hkv] arrival counters (0 between launches)
+    int cluster;                       // the S CTAs of a (b, g) are one thread-block cluster:
+                                       // partial states combined through distributed shared memory
 };
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// A float at shared address `a` (this CTA's layout) in cluster CTA `rank`.
+__device__ __forceinline__ float ld_cluster_f32(uint32_t a, uint32_t rank) {
+    uint32_t ra;
+    float v;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
+    return v;
+}
 
 template <typename T, int D, int G, bool ROPE>
 __global__ void __launch_bounds__(D) k_attn_decode(const T *q, T *k_cache, T *v_cache,
@@ -416,8 +431,41 @@ __global__ void __launch_bounds__(D) k_attn_decode(const T *q, T *k_cache, T *v_
         for (int h = 0; h < G; ++h) ob[h * D + i] = from_f32<T>(n > 0 ? acc[h] / stat[h][1] : 0.f);
         return;
     }
-    // this chunk's (m, l, acc) -> the workspace; the last CTA of (b, g) combines
     constexpr int PW = G * D + 2 * G;
+    if (sp.cluster) {
+        // this chunk's (m, l, acc) in shared memory; after a cluster barrier
+        // CTA s of the (b, g) cluster combines outputs [s * per, (s + 1) * per)
+        // of the G * D from every chunk's state (chunk order, the arithmetic of
+        // the workspace combine below), then a second barrier keeps every
+        // CTA's state alive until all have read it
+        __shared__ float cst[PW];
+#pragma unroll
+        for (int h = 0; h < G; ++h) cst[h * D + i] = acc[h];
+        if (i < G) {
+            cst[G * D + i] = nc > 0 ? stat[i][0] : -INFINITY;
+            cst[G * D + G + i] = nc > 0 ? stat[i][1] : 0.f;
+        }
+        cluster_sync_all();
+        const uint32_t cb = smem_u32(cst);
+        const int per = (G * D + S - 1) / S;
+        const int e1 = min((s + 1) * per, G * D);
+        for (int e = s * per + (int)threadIdx.x; e < e1; e += D) {
+            const int h = e / D;
+            float M = -INFINITY;
+            for (int t = 0; t < S; ++t) M = fmaxf(M, ld_cluster_f32(cb + 4u * (G * D + h), (uint32_t)t));
+            float lsum = 0.f, o = 0.f;
+            for (int t = 0; t < S; ++t) {
+                const float mt = ld_cluster_f32(cb + 4u * (G * D + h), (uint32_t)t);
+                const float f = mt == -INFINITY ? 0.f : expf(mt - M);
+                lsum = fmaf(ld_cluster_f32(cb + 4u * (G * D + G + h), (uint32_t)t), f, lsum);
+                o = fmaf(ld_cluster_f32(cb + 4u * e, (uint32_t)t), f, o);
+            }
+            ob[e] = from_f32<T>(lsum > 0.f ? o / lsum : 0.f);
+        }
+        cluster_sync_all();
+        return;
+    }
+    // this chunk's (m, l, acc) -> the workspace; the last CTA of (b, g) combines
     float *pp = sp.part + ((int64_t)bg * S + s) * PW;
 #pragma unroll
     for (int h = 0; h < G; ++h) pp[h * D + i] = acc[h];
@@ -714,7 +762,7 @@ int launch_attn(const void *q_dev, void *k_cache_dev, void *v_cache_dev, int dty
     int S = ws ? attn_splits(B, Hkv, cache_len) : 1;
     if (ws && ws_bytes < attn_workspace_bytes(B, Hkv, G, head_dim, S)) return CBQ_ERR_ARG;
     if (B * Hkv * S > 0x7fffffff) return CBQ_ERR_ARG;
-    AttnSplit sp{S, (int)((cache_len + S - 1) / S), nullptr, nullptr};
+    AttnSplit sp{S, (int)((cache_len + S - 1) / S), nullptr, nullptr, 0};
     if (S > 1) {
         sp.part = static_cast<float *>(ws);
         sp.count = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(ws) +
@@ -722,8 +770,13 @@ int launch_attn(const void *q_dev, void *k_cache_dev, void *v_cache_dev, int dty
     }
     // scores of the group's heads; the combining CTA reuses it for 3 * S * G chunk values
     const size_t smem = std::max((size_t)sp.cmax * 4 * (size_t)G, (size_t)(S > 1 ? 3 * S * G * 4 : 0));
-    if (smem > (size_t)cbq_host::max_smem_optin() - 4096 - (ROPE ? (size_t)G * head_dim * 4 : 0))
+    if (smem > (size_t)cbq_host::max_smem_optin() - 4096 - (size_t)(G * head_dim + 2 * G) * 4 -
+                   (ROPE ? (size_t)G * head_dim * 4 : 0))
         return CBQ_ERR_UNSUPPORTED;
+    // up to 16 chunks: the chunks of a (row, kv head) form one thread-block
+    // cluster and combine through distributed shared memory (no workspace
+    // round trip); a launch the device refuses falls back to the workspace
+    const bool try_cluster = S >= 2 && S <= 16 && cbq_host::attn_cluster_enabled();
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const dim3 grid((unsigned)(B * Hkv * S));
 #define CBQ_AT(T, D, GG)                                                                             \
@@ -733,10 +786,23 @@ int launch_attn(const void *q_dev, void *k_cache_dev, void *v_cache_dev, int dty
             CBQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
         const AttnRope<T> rp{static_cast<const T *>(k_dev), static_cast<const T *>(v_dev), qw, kw,  \
                              cos_dev, sin_dev, eps};                                                 \
-        CBQ_CUDA_TRY(cbq_host::launch_pdl(kern, grid, dim3(D), smem, s, static_cast<const T *>(q_dev), \
-                                          static_cast<T *>(k_cache_dev), static_cast<T *>(v_cache_dev), \
-                                          pos_dev, (int)Hq, (int)Hkv, cache_len, scale,              \
-                                          static_cast<T *>(out_dev), rp, sp));                       \
+        bool done = false;                                                                           \
+        if (try_cluster && (S <= 8 || cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, \
+                                                           1) == cudaSuccess)) {                     \
+            AttnSplit spc = sp;                                                                      \
+            spc.cluster = 1;                                                                         \
+            done = cbq_host::launch_pdl_cluster(kern, grid, dim3(D), smem, (unsigned)S, s,           \
+                                                static_cast<const T *>(q_dev), static_cast<T *>(k_cache_dev), \
+                                                static_cast<T *>(v_cache_dev), pos_dev, (int)Hq, (int)Hkv, \
+                                                cache_len, scale, static_cast<T *>(out_dev), rp, spc) == \
+                   cudaSuccess;                                                                      \
+            if (!done) (void)cudaGetLastError();                                                     \
+        }                                                                                            \
+        if (!done)                                                                                   \
+            CBQ_CUDA_TRY(cbq_host::launch_pdl(kern, grid, dim3(D), smem, s, static_cast<const T *>(q_dev), \
+                                              static_cast<T *>(k_cache_dev), static_cast<T *>(v_cache_dev), \
+                                              pos_dev, (int)Hq, (int)Hkv, cache_len, scale,          \
+                                              static_cast<T *>(out_dev), rp, sp));                   \
     } while (0)
 #define CBQ_AT_G(T, D)                                                                               \
     do {                                                                                             \

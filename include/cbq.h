@@ -506,9 +506,12 @@ int64_t cbq_attn_workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int64_t hea
  * head) split over several CTAs (flash-decoding): each CTA attends over one
  * chunk of the keys and writes its partial softmax state (max, sum,
  * unnormalised weighted values) to the workspace, and the CTA that finishes
- * a (row, kv head) last combines the chunks in chunk order.  The number of
- * chunks depends only on B, Hkv, cache_len and the SM count, so a call is
- * deterministic.  Results equal the one-CTA forms up to the fp32 summation
+ * a (row, kv head) last combines the chunks in chunk order; with at most 16
+ * chunks they run as one thread-block cluster and combine through
+ * distributed shared memory instead (same arithmetic and order;
+ * CBQ_ATTN_CLUSTER=0 in the environment selects the workspace form).  The
+ * number of chunks depends only on B, Hkv, cache_len and the SM count, so a
+ * call is deterministic.  Results equal the one-CTA forms up to the fp32 summation
  * order.  workspace_bytes >= cbq_attn_workspace_bytes(...), else CBQ_ERR_ARG.
  * Calls that share a workspace must not overlap on the GPU.  No counterpart
  * in the reference (HF attention on the host framework's side). */
