@@ -83,6 +83,7 @@ SIGNATURES = {
     "cbq_attn_decode": (_INT, [_P, _P, _P, _INT, _I64, _I64, _I64, _I64, _I64, _P, ct.c_float, _P, _P]),
     "cbq_attn_decode_rope": (_INT, [_P, _P, _P, _INT, _I64, _I64, _I64, _I64, ct.c_float, _P, _P, _P, _P, _P,
                                     _P, _P, _I64, ct.c_float, _P, _P]),
+    "cbq_silu_mul": (_INT, [_P, _P, _INT, _I64, _P, _P]),
     "cbq_attn_workspace_bytes": (_I64, [_I64, _I64, _I64, _I64, _I64]),
     "cbq_attn_decode_rope_split": (_INT, [_P, _P, _P, _INT, _I64, _I64, _I64, _I64, ct.c_float, _P, _P, _P, _P,
                                           _P, _P, _P, _I64, ct.c_float, _P, _P, _I64, _P]),

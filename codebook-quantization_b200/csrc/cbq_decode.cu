@@ -616,6 +616,20 @@ __global__ void __launch_bounds__(1024) k_greedy_pick(const T *logits, int64_t V
     next_ids[b] = id;
 }
 
+// out[i] = round(round(silu(g[i])) * u[i]) (g, u already rounded to T): the
+// SiLU * up of a transformer MLP when gate and up were computed separately,
+// with the rounding of the torch sequence (and of the GEMV epilogue).
+template <typename T>
+__global__ void __launch_bounds__(256) k_silu_mul(const T *g, const T *u, int64_t n, T *out) {
+    pdl_launch_dependents();
+    pdl_wait();
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float gv = to_f32<T>(g[i]), uv = to_f32<T>(u[i]);
+        const float sv = to_f32<T>(from_f32<T>(gv / (1.0f + expf(-gv))));
+        out[i] = from_f32<T>(sv * uv);
+    }
+}
+
 }  // namespace
 
 // ------------------------------------------------------------------- C ABI
@@ -880,4 +894,23 @@ extern "C" int cbq_attn_decode_split(const void *q_dev, const void *k_cache_dev,
     return launch_attn<false>(q_dev, const_cast<void *>(k_cache_dev), const_cast<void *>(v_cache_dev), dtype, B,
                               Hq, Hkv, head_dim, cache_len, pos_dev, scale, out_dev, nullptr, nullptr, nullptr,
                               nullptr, nullptr, nullptr, 0.f, workspace_dev, workspace_bytes, stream);
+}
+
+extern "C" int cbq_silu_mul(const void *g_dev, const void *u_dev, int dtype, int64_t n, void *out_dev,
+                            void *stream) {
+    if (n < 0 || (dtype != CBQ_F32 && dtype != CBQ_BF16)) return CBQ_ERR_ARG;
+    if (n == 0) return CBQ_OK;
+    if (!g_dev || !u_dev || !out_dev) return CBQ_ERR_ARG;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const unsigned blocks = (unsigned)std::min<int64_t>((n + 255) / 256, (int64_t)cbq_host::sm_count() * 4);
+    if (dtype == CBQ_F32)
+        CBQ_CUDA_TRY(cbq_host::launch_pdl(k_silu_mul<float>, dim3(blocks), dim3(256), 0, s,
+                                          static_cast<const float *>(g_dev), static_cast<const float *>(u_dev), n,
+                                          static_cast<float *>(out_dev)));
+    else
+        CBQ_CUDA_TRY(cbq_host::launch_pdl(k_silu_mul<__nv_bfloat16>, dim3(blocks), dim3(256), 0, s,
+                                          static_cast<const __nv_bfloat16 *>(g_dev),
+                                          static_cast<const __nv_bfloat16 *>(u_dev), n,
+                                          static_cast<__nv_bfloat16 *>(out_dev)));
+    return CBQ_OK;
 }

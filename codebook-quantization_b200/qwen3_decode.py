@@ -203,6 +203,8 @@ class Qwen3Decoder:
             self.q, self.k, self.v = z(hq), z(hkv), z(hkv)
             self.a, self.qn = z(hq), (None if fuse_rope else z(hq))
             self.m = z(cfg.inter // self.world)
+            # gate and up computed by separate launches (Huffman, batch > 2)
+            self.gm, self.um = z(cfg.inter // self.world), z(cfg.inter // self.world)
             self.logits_buf = z(cfg.vocab // self.world)
             self.code = _lib.CBQ_BF16 if act_dtype == torch.bfloat16 else _lib.CBQ_F32
             # arrival count of the GEMVs whose last CTA normalises (0 between launches)
@@ -279,8 +281,12 @@ class Qwen3Decoder:
                 return
             if rc != _lib.CBQ_ERR_UNSUPPORTED:
                 raise _lib.CbqError("cbq_linear_fixed_residual_norm", rc)
-        self._linear((lin,), (self.x,), _lib.CBQ_EPI_RESIDUAL, (self.x,), x=x)
-        self._rmsnorm(self.x, self.h)
+        fixed = isinstance(lin, GPUAcceleratedLinear)
+        if fixed and linear_fixed_multi((lin,), x, (self.x,), _lib.CBQ_EPI_RESIDUAL, (self.x,)):
+            self._rmsnorm(self.x, self.h)
+            return
+        lin(x, out=self.y)                   # separate launch: the norm launch adds the residual
+        self._rmsnorm(self.x, self.h, add=self.y)
 
     def _linear(self, mats, outs, epilogue=_lib.CBQ_EPI_STORE, resids=None, x=None):
         x = self.h if x is None else x
@@ -289,8 +295,14 @@ class Qwen3Decoder:
             return
         # matrices one by one (Huffman streams, or shapes outside the fused kernel)
         if epilogue == _lib.CBQ_EPI_SILU_MUL:
-            g, u = mats[0](x), mats[1](x)
-            outs[0].copy_(F.silu(g) * u)
+            if outs[0] is self.m and x.dtype == self.dt:
+                mats[0](x, out=self.gm)
+                mats[1](x, out=self.um)
+                _lib.call("cbq_silu_mul", self.gm.data_ptr(), self.um.data_ptr(), self.code, self.m.numel(),
+                          self.m.data_ptr(), device_stream(self.dev))
+            else:
+                g, u = mats[0](x), mats[1](x)
+                outs[0].copy_(F.silu(g) * u)
         elif epilogue == _lib.CBQ_EPI_RESIDUAL:
             for m, o, r in zip(mats, outs, resids):
                 o.copy_(r + m(x))
@@ -453,8 +465,8 @@ class Qwen3Decoder:
         if self.prenorm or self.peer_prenorm:   # embedding, 5 per layer (norms inside the GEMVs), lm_head, pick
             return 1 + 5 * n + 2
         pick = 1 if (self.world == 1 or self.peer is not None) else 0   # cbq_greedy_pick
-        if self.w.huffman or self.B > 2:  # one launch per linear, separate RMSNorms
-            per = 3 + attn + 1 + 2 + 1 + 2
+        if self.w.huffman or self.B > 2:  # one launch per linear, separate RMSNorms (+ residual), SiLU * up
+            per = 3 + attn + 1 + 1 + 2 + 1 + 1 + 1
         elif (self.world == 1 or self.peer is not None) and self.fuse_norm:
             per = 4 + attn                # q/k/v, attention, o (+norm), gate/up, down (+norm)
         else:
@@ -472,7 +484,7 @@ class Qwen3Decoder:
             return (f"q/k/v (+ all-reduce of down, norm), {attn}, o (partial rows to every rank), "
                     f"gate/up (+ all-reduce of o, norm, SiLU*up), down (partial rows to every rank)")
         if self.w.huffman or self.B > 2:
-            return f"q, k, v, {attn}, o, norm, gate, up, down, norm"
+            return f"q, k, v, {attn}, o, residual + norm, gate, up, SiLU*up, down, residual + norm"
         norm = " + norm" if self.fuse_norm else ", norm"
         ar = " (peer all-reduce)" if self.peer is not None else (" + NCCL all-reduce" if self.world > 1 else "")
         return f"q/k/v, {attn}, o{ar}{norm}, gate/up, down{ar}{norm}"

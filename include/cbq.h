@@ -502,6 +502,12 @@ int cbq_attn_decode_rope(const void *q_dev, const void *k_dev, const void *v_dev
  * leaves them zero).  No counterpart in the reference. */
 int64_t cbq_attn_workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int64_t head_dim, int64_t cache_len);
 
+/* out[i] = round(round(silu(g[i])) * u[i]) over n elements (fp32 or bf16;
+ * out may alias g or u): SiLU * up when gate and up come from separate
+ * launches (Huffman streams, more than two tokens), with the rounding of the
+ * fused GEMV epilogue.  No counterpart in the reference (HF Qwen3MLP). */
+int cbq_silu_mul(const void *g_dev, const void *u_dev, int dtype, int64_t n, void *out_dev, void *stream);
+
 /* cbq_attn_decode_rope / cbq_attn_decode with the keys of every (row, kv
  * head) split over several CTAs (flash-decoding): each CTA attends over one
  * chunk of the keys and writes its partial softmax state (max, sum,

@@ -442,3 +442,25 @@ def test_greedy_pick_equals_torch_argmax(dt):
     v0, i0 = lg[:, :Vh].float().max(dim=-1)                           # what rank 0 published
     got = bufs[1, :B * 2].view(B, 2)
     assert torch.equal(got[:, 1] & 0xFFFFFFFF, i0) and bool(((got >> 32) == 5).all())
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+def test_silu_mul_equals_torch(dt):
+    """cbq_silu_mul (SiLU * up of separately computed gate and up rows) is
+    bit-identical to torch's F.silu(g) * u in the same dtype, out of place
+    and in place."""
+    import torch.nn.functional as F
+    dev = need_cuda()
+    n = 3 * 12288 + 5
+    g = (torch.randn(n, device=dev) * 3).to(dt)
+    u = torch.randn(n, device=dev).to(dt)
+    code = L.CBQ_BF16 if dt == torch.bfloat16 else L.CBQ_F32
+    st = torch.cuda.current_stream(dev).cuda_stream
+    out = torch.empty_like(g)
+    L.call("cbq_silu_mul", g.data_ptr(), u.data_ptr(), code, n, out.data_ptr(), st)
+    want = F.silu(g) * u
+    torch.cuda.synchronize()
+    assert torch.equal(out, want)
+    L.call("cbq_silu_mul", g.data_ptr(), u.data_ptr(), code, n, g.data_ptr(), st)     # out aliases g
+    torch.cuda.synchronize()
+    assert torch.equal(g, want)
