@@ -21,9 +21,18 @@ CFG = cbq.qwen3.Qwen3Config("tiny-tp", 2, 256, 512, 4, 2, 64, 1000, 1e6, False)
 
 
 def _free_port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+    """A bindable port below the kernel's ephemeral range, so that a port an
+    earlier test's connections still hold (TIME_WAIT) is not handed out."""
+    import random
+    for _ in range(100):
+        port = random.randrange(20000, 30000)
+        with socket.socket() as s:
+            try:
+                s.bind(("127.0.0.1", port))
+            except OSError:
+                continue
+            return port
+    raise RuntimeError("no free port")
 
 
 def _prompt():
@@ -78,20 +87,23 @@ def test_tp2_decode_matches_one_gpu(fused, allreduce, fuse_norm, huffman):
         _prompt(), 12).cpu().tolist()
     del W
     ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, fused, huffman, q, allreduce, fuse_norm))
-             for r in range(2)]
-    for p in procs:
-        p.start()
-    res = {}
-    for _ in procs:
-        r, msg, eager, graphed = q.get(timeout=300)
-        res[r] = (msg, eager, graphed)
-    for p in procs:
-        p.join(timeout=60)
-        if p.is_alive():
-            p.kill()
+    for attempt in range(3):                    # a rendezvous port taken meanwhile: another port
+        q = ctx.Queue()
+        port = _free_port()
+        procs = [ctx.Process(target=_rank_main, args=(r, 2, port, fused, huffman, q, allreduce, fuse_norm))
+                 for r in range(2)]
+        for p in procs:
+            p.start()
+        res = {}
+        for _ in procs:
+            r, msg, eager, graphed = q.get(timeout=300)
+            res[r] = (msg, eager, graphed)
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+        if not any("EADDRINUSE" in str(m[0]) for m in res.values()):
+            break
     for r in range(2):
         msg, eager, graphed = res[r]
         assert msg == "ok", (r, msg)

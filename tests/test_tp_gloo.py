@@ -21,9 +21,18 @@ M, K, BITS_SEED = 192, 768, 21
 
 
 def _free_port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+    """A bindable port below the kernel's ephemeral range, so that a port an
+    earlier test's connections still hold (TIME_WAIT) is not handed out."""
+    import random
+    for _ in range(100):
+        port = random.randrange(20000, 30000)
+        with socket.socket() as s:
+            try:
+                s.bind(("127.0.0.1", port))
+            except OSError:
+                continue
+            return port
+    raise RuntimeError("no free port")
 
 
 def _matrix(kind: str):
