@@ -90,6 +90,9 @@ def parse():
 # (kernel, M, K, tokens); shapes not captured report null.
 NCU_TRAFFIC = {
     ("k_gemv_fixed", 12288, 4096, 1): 81.880832e6 + 2.562048e6,
+    ("k_gemv_fixed", 6144, 4096, 1): 40.997376e6,          # gate_proj rows of one rank at TP2
+    ("k_gemv_fixed", 3072, 4096, 1): 20.549120e6,          # TP4
+    ("k_gemv_fixed", 1536, 4096, 1): 10.324736e6,          # TP8
     ("k_gemv_huff", 12288, 4096, 1): 72.563456e6 + 1.255424e6,
 }
 
