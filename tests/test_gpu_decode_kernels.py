@@ -464,3 +464,47 @@ def test_silu_mul_equals_torch(dt):
     L.call("cbq_silu_mul", g.data_ptr(), u.data_ptr(), code, n, g.data_ptr(), st)     # out aliases g
     torch.cuda.synchronize()
     assert torch.equal(g, want)
+
+
+_ATTN_SCRIPT = r"""
+import sys, numpy as np, torch
+from pathlib import Path
+sys.path.insert(0, str(Path(sys.argv[1]).parent))
+sys.path.insert(0, sys.argv[1])
+from helpers import cbq
+L = cbq._lib
+B, Hq, Hkv, d, Lc, pos = 1, 32, 8, 128, 200, 171
+g = torch.Generator().manual_seed(17)
+dev = torch.device("cuda", 0)
+q = torch.randn(B, Hq, d, generator=g).to(dev).to(torch.bfloat16)
+kc = torch.randn(B, Hkv, Lc, d, generator=g).to(dev).to(torch.bfloat16)
+vc = torch.randn(B, Hkv, Lc, d, generator=g).to(dev).to(torch.bfloat16)
+p = torch.tensor([pos], device=dev)
+nws = L.query("cbq_attn_workspace_bytes", B, Hq, Hkv, d, Lc)
+ws = torch.zeros(nws, dtype=torch.uint8, device=dev)
+out = torch.empty(B, Hq * d, device=dev, dtype=torch.bfloat16)
+L.call("cbq_attn_decode_split", q.data_ptr(), kc.data_ptr(), vc.data_ptr(), L.CBQ_BF16, B, Hq, Hkv, d, Lc,
+       p.data_ptr(), d ** -0.5, out.data_ptr(), ws.data_ptr(), nws, torch.cuda.current_stream(dev).cuda_stream)
+torch.cuda.synchronize()
+np.save(sys.argv[2], out.view(torch.int16).cpu().numpy())
+"""
+
+
+def test_attn_cluster_combine_equals_workspace_combine(tmp_path):
+    """The cluster combine (distributed shared memory) and the workspace
+    combine (global partial states, last CTA) do the same arithmetic in the
+    same chunk order: bit-identical outputs.  Each form runs in its own
+    process (CBQ_ATTN_CLUSTER is read once per process)."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+    need_cuda()
+    here = str(Path(__file__).resolve().parent)
+    outs = []
+    for flag in ("1", "0"):
+        f = tmp_path / f"attn_{flag}.npy"
+        env = dict(os.environ, CBQ_ATTN_CLUSTER=flag)
+        subprocess.run([sys.executable, "-c", _ATTN_SCRIPT, here, str(f)], env=env, check=True, timeout=300)
+        outs.append(np.load(f))
+    assert np.array_equal(outs[0], outs[1])
